@@ -1,0 +1,548 @@
+"""Benchmark of vk-compute's decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Default workload (N=1 headline): RmsNorm-GEMV INT8 -- x 4096 ~N(0,1), gamma
+~1+N(0,0.1), eps 1e-6, W 12288x4096 ~N(0,0.02) symmetric int8 with fp16-valued
+scales in the reference storage (per (k, 256-output block) fp32 scale/zero,
+16-byte chunk packing).  A step is one fused RmsNorm-GEMV over one weight
+matrix; steps rotate through a pool of weight copies larger than 4x L2 so
+every step streams its weights from HBM.  Steps are captured in a CUDA
+graph (one launch per step).
+
+Metric: achieved HBM GB/s = algorithmic bytes (weights, scales and zeros
+once, activations in and out once) / device time per step.  With
+torchrun (N>1) every rank holds its own row shard of a 12288N x 4096
+matrix (weak scaling, no collective on the data path) and `value` is the
+total over ranks, timed as the max over ranks.
+
+--impl reference times the reference's CPU algorithm (the oracle's C port of
+src/compute.c's loops over the src/data.c storage, all host threads) on the
+same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "rmsnorm_gemv_int8": "RmsNorm-GEMV INT8 12288x4096 (x 4096, eps 1e-6, symmetric int8, fp16-valued scales)",
+    "gemv_fp16": "GEMV FP16 4096x4096 (x 4096)",
+    "swiglu_ffn_int4": "RmsNorm-swiglu-ffn INT4 gate/up 12288x4096 + down GEMV INT4 4096x12288",
+    "qkv_rope_attn_int4": "RmsNorm-GEMV-Rope INT4 QKV 6144x4096 (theta 1e6) + Att-full-FP16 32q/8kv x 128, ctx 8192",
+}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(workload)
+    return None if v is None else v.get("bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"vkc_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append({"sm": float(parts[1]), "max": float(parts[2]), "power": float(parts[3]),
+                             "hw": parts[5], "hw_thermal": parts[6], "sw_thermal": parts[7], "power_cap": parts[8]})
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
+                              ("sw_thermal", "sw_thermal_slowdown"), ("power_cap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [r for r in rows if r["power"] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+# ---------------------------------------------------------------------------
+# Workloads (our implementation)
+# ---------------------------------------------------------------------------
+
+def build_workload(name: str, rank: int, device):
+    """Returns (step_fn(i), bytes_per_step, launches_per_step, dominant(i),
+    dominant_bytes, e2e, meta).  step_fn(i) enqueues step i on the current
+    stream."""
+    import torch
+
+    from vk_compute_b200 import ops
+
+    gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
+
+    def randn(*shape, std=1.0, mean=0.0):
+        return (torch.randn(*shape, generator=gen) * std + mean).to(device)
+
+    def pool_of(make, nbytes):
+        n = max(2, min(64, math.ceil(4 * L2_BYTES / nbytes)))
+        base = [make(j) for j in range(min(n, 4))]
+        return [base[j % len(base)] if j < len(base) else clone(base[j % len(base)]) for j in range(n)]
+
+    def clone(w):
+        return ops.PackedWeight(w.bits, w.K, w.N, w.packed.clone(),
+                                None if w.scale is None else w.scale.clone(),
+                                None if w.zero is None else w.zero.clone())
+
+    if name in ("rmsnorm_gemv_int8", "gemv_fp16"):
+        if name == "rmsnorm_gemv_int8":
+            K, N, bits = 4096, 12288, 8
+        else:
+            K, N, bits = 4096, 4096, 16
+        x = randn(K)
+        gamma = randn(K, std=0.1, mean=1.0)
+        y = torch.empty(N, device=device)
+        wbytes = K * N * bits // 8 + (2 * 4 * K * N // 256 if bits <= 8 else 0)
+        pool = pool_of(lambda j: ops.pack_dense(randn(K, N, std=0.02), bits, symmetric=True, fp16_scale=True),
+                       wbytes)
+        if name == "rmsnorm_gemv_int8":
+            act = 4 * K * 2 + 4 * N  # x, gamma in; y out
+            step = lambda i: ops.rmsnorm_gemv(pool[i % len(pool)], x, gamma, eps=1e-6, out=y)
+        else:
+            act = 4 * K + 4 * N
+            step = lambda i: ops.gemv(pool[i % len(pool)], x, out=y)
+        meta = {"K": K, "N": N, "bits": bits, "pool": len(pool), "pool_bytes": len(pool) * wbytes}
+        return dict(step=step, bytes=wbytes + act, launches=1, dominant=step, dominant_bytes=wbytes + act,
+                    dominant_name=("RmsNorm-GEMV-INT8" if bits == 8 else "GEMV-FP16"), meta=meta,
+                    e2e=(pool, x, gamma, y, K, N, bits))
+
+    if name == "swiglu_ffn_int4":
+        H, I = 4096, 12288
+        x = randn(H)
+        gamma = randn(H, std=0.1, mean=1.0)
+        h = torch.empty(I, device=device)
+        out = torch.empty(H, device=device)
+        gu_bytes = 2 * (H * I // 2 + 2 * 4 * H * I // 256)
+        d_bytes = I * H // 2 + 2 * 4 * I * H // 256
+        layer_bytes = gu_bytes + d_bytes
+        n = max(2, min(32, math.ceil(4 * L2_BYTES / layer_bytes)))
+        layers = []
+        for j in range(n):
+            if j < 2:
+                layers.append((ops.pack_dense(randn(H, I, std=0.02), 4), ops.pack_dense(randn(H, I, std=0.02), 4),
+                               ops.pack_dense(randn(I, H, std=0.02), 4)))
+            else:
+                layers.append(tuple(clone(w) for w in layers[j % 2]))
+
+        def step(i):
+            g, u, d = layers[i % n]
+            ops.rmsnorm_swiglu(g, u, x, gamma, eps=1e-6, out=h)
+            ops.gemv(d, h, out=out)
+
+        dom = lambda i: ops.rmsnorm_swiglu(*layers[i % n][:2], x, gamma, eps=1e-6, out=h)
+        act = 4 * H * 2 + 4 * I + 4 * I + 4 * H
+        return dict(step=step, bytes=layer_bytes + act, launches=2, dominant=dom,
+                    dominant_bytes=gu_bytes + 4 * H * 2 + 4 * I, dominant_name="RmsNorm-swiglu-ffn-INT4",
+                    meta={"hidden": H, "intermediate": I, "pool": n}, e2e=None)
+
+    if name == "qkv_rope_attn_int4":
+        H, NQ, NKV, HD, CTX = 4096, 32, 8, 128, 8192
+        NQKV = (NQ + 2 * NKV) * HD
+        x = randn(H)
+        gamma = randn(H, std=0.1, mean=1.0)
+        theta = (1e6 ** (-torch.arange(HD // 2, dtype=torch.float64) * 2 / HD)).float().to(device)
+        qkv = torch.empty(NQKV, device=device)
+        att = torch.empty(NQ * HD, device=device)
+        wbytes = H * NQKV // 2 + 2 * 4 * H * NQKV // 256
+        kvbytes = 2 * CTX * NKV * HD * 2
+        n = max(2, min(32, math.ceil(4 * L2_BYTES / (wbytes + kvbytes))))
+        layers = []
+        for j in range(n):
+            if j < 2:
+                w = ops.pack_dense(randn(H, NQKV, std=0.02), 4)
+                kc = randn(CTX, NKV, HD).half()
+                vc = randn(NKV, HD // 8, CTX, 8).half()
+                layers.append((w, kc, vc))
+            else:
+                w, kc, vc = layers[j % 2]
+                layers.append((clone(w), kc.clone(), vc.clone()))
+        ws = ops.attention_workspace(NQ, NKV, HD, CTX, device=device)
+        pos = int(torch.randint(0, 8192, (1,), generator=gen))
+
+        def step(i):
+            w, kc, vc = layers[i % n]
+            ops.rmsnorm_gemv_rope(w, x, gamma, theta, pos, mode="pairs", head_dim=HD, rot_rows=(NQ + NKV) * HD,
+                                  eps=1e-6, out=qkv)
+            ops.attention_decode(qkv[:NQ * HD], kc, vc, NQ, NKV, HD, CTX, 1 / math.sqrt(HD), workspace=ws, out=att)
+
+        dom = lambda i: ops.attention_decode(qkv[:NQ * HD], layers[i % n][1], layers[i % n][2], NQ, NKV, HD, CTX,
+                                             1 / math.sqrt(HD), workspace=ws, out=att)
+        act = 4 * H * 2 + 4 * NQKV + 4 * NQ * HD * 2
+        return dict(step=step, bytes=wbytes + kvbytes + act, launches=2, dominant=dom,
+                    dominant_bytes=kvbytes + 4 * NQ * HD * 2, dominant_name="Att-full-FP16",
+                    meta={"pool": n, "pos": pos, "ctx": CTX}, e2e=None)
+    raise SystemExit(f"unknown workload {name}; choose from {sorted(WORKLOADS)}")
+
+
+def capture(fn, count, start=0):
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(start)  # one eager call on the capture stream before capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        for i in range(count):
+            fn(start + i)
+    return g
+
+
+def e2e_dropin(args, e2e, device_index):
+    """Same metric through the reference-facing C ABI with host buffers:
+    per step writeBuffer(x) from pinned host memory, execute() of the
+    operator by its shader name, readBuffer(y)."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    from vk_compute_b200 import dropin as D
+
+    pool, x, gamma, y, K, N, bits = e2e
+    os.environ["VKC_DEVICE"] = str(device_index)
+    s = D.create_session()
+    L = D.abi()
+
+    def dev_buffer(t: torch.Tensor):
+        h = t.cpu().numpy()
+        return D.create_buffer(s, h)
+
+    bufs = [(dev_buffer(w.packed), dev_buffer(w.scale), dev_buffer(w.zero)) for w in pool[:max(2, len(pool))]]
+    x_host = torch.empty(K, dtype=torch.float32).pin_memory()
+    x_host.copy_(x.cpu())
+    y_host = torch.empty(N, dtype=torch.float32).pin_memory()
+    xb = D.create_buffer(s, x_host.numpy())
+    gb = D.create_buffer(s, gamma.cpu().numpy())
+    yb = D.create_buffer(s, None, 4 * N)
+    name = "RmsNorm-GEMV-INT8.spv" if bits == 8 else "GEMV-FP16.spv"
+    ops_ = []
+    for wb, sb, zb in bufs:
+        if bits == 8:
+            ops_.append(D.operation(name, [xb, gb, wb, yb, sb, zb], [1, N, K]))
+        else:
+            ops_.append(D.operation(name, [xb, wb, yb], [1, N, K]))
+    arrs = [(D.Operation * 1)(op) for op in ops_]
+    xp = C.c_void_p(x_host.data_ptr())
+    yp = C.c_void_p(y_host.data_ptr())
+
+    def one(i):
+        L.writeBuffer(s.dev.device, s.dev.queue, xb, xp)
+        L.execute(s, arrs[i % len(arrs)], 1)
+        L.readBuffer(s.dev.device, s.dev.physicalDevice, s.dev.queue, yb, yp)
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(i)
+    dt = (time.perf_counter() - t0) / args.steps
+    for wb, sb, zb in bufs:
+        for b in (wb, sb, zb):
+            D.destroy_buffer(s, b)
+    for b in (xb, gb, yb):
+        D.destroy_buffer(s, b)
+    D.destroy_session(s)
+    return dt, 4 * K, 4 * N
+
+
+def cpu_baseline(workload: str, budget_s: float = 12.0, threads: int | None = None):
+    """The reference's CPU algorithm (oracle port of src/compute.c:216-290
+    over the src/data.c storage) on a bounded sample of the workload."""
+    import numpy as np
+
+    from oracle import pyoracle as o
+
+    threads = threads or len(os.sched_getaffinity(0))
+    o.set_threads(threads)
+    rng = np.random.default_rng(0)
+    if workload == "rmsnorm_gemv_int8":
+        K, N, bits = 4096, 12288, 8
+    elif workload == "gemv_fp16":
+        K, N, bits = 4096, 4096, 16
+    elif workload == "swiglu_ffn_int4":
+        K, N, bits = 4096, 12288, 4
+    else:
+        K, N, bits = 4096, 6144, 4
+    w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02)
+    x = rng.standard_normal(K, dtype=np.float32)
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    if bits == 16:
+        data, s, z = w.astype(np.float16).view(np.uint16), None, None
+        nbytes = K * N * 2 + 8 * K
+    else:
+        data, s, z = o.quantize(w, bits, True, True)
+        nbytes = K * N * bits // 8 + 8 * K * N // 256 + 8 * K + 4 * N
+    gamma = None if workload == "gemv_fp16" else g
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        if workload == "swiglu_ffn_int4":
+            o.qswiglu(x, g, (data, s, z), (data, s, z), bits, K, N, K, 1e-6)
+        else:
+            o.qgemv(x, gamma, data, s, z, bits, K, N, K, 1e-6)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 1000:
+            break
+    per = el / reps
+    mult = 2 if workload == "swiglu_ffn_int4" else 1
+    return {"value": round(mult * nbytes / per / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full passes of {bits}-bit {K}x{N}{' gate+up' if mult == 2 else ''} in {el:.1f} s",
+            "s_per_pass": per}
+
+
+def run_reference(args, rank, world):
+    """The reference arm: W untimed then K timed passes of the reference's
+    CPU algorithm over the whole workload, all host threads."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import pyoracle as o
+
+    wl = args.workload
+    threads = len(os.sched_getaffinity(0))
+    o.set_threads(threads)
+    K, N, bits = {"rmsnorm_gemv_int8": (4096, 12288, 8), "gemv_fp16": (4096, 4096, 16),
+                  "swiglu_ffn_int4": (4096, 12288, 4), "qkv_rope_attn_int4": (4096, 6144, 4)}[wl]
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((K, N), dtype=np.float32) * 0.02
+    x = rng.standard_normal(K, dtype=np.float32)
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    if bits == 16:
+        data, s, z = w.astype(np.float16).view(np.uint16), None, None
+        nbytes = K * N * 2 + 4 * K + 4 * N
+    else:
+        data, s, z = o.quantize(w, bits, True, True)
+        nbytes = K * N * bits // 8 + 8 * K * N // 256 + 8 * K + 4 * N
+    gamma = None if wl == "gemv_fp16" else g
+
+    def one():
+        if wl == "swiglu_ffn_int4":
+            o.qswiglu(x, g, (data, s, z), (data, s, z), bits, K, N, K, 1e-6)
+        else:
+            o.qgemv(x, gamma, data, s, z, bits, K, N, K, 1e-6)
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    per = (time.perf_counter() - t0) / args.steps
+    if wl == "swiglu_ffn_int4":
+        nbytes = 2 * nbytes
+    value = round(nbytes / per / 1e9, 4)
+    sample = f"{args.steps} full passes of the {bits}-bit {K}x{N} operator ({nbytes} B each)"
+    line = {"impl": "reference", "metric": f"{WORKLOADS[wl]} achieved HBM GB/s", "value": value,
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl, "description": WORKLOADS[wl]},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="rmsnorm_gemv_int8", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-graph", action="store_true", help="launch steps eagerly instead of from a CUDA graph")
+    ap.add_argument("--no-pdl", action="store_true", help="plain launches (no programmatic dependent launch)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clock-window", type=float, default=1.5, help="seconds of sampled load before timing")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from vk_compute_b200 import ops
+
+    ops.set_pdl(not args.no_pdl)
+    wl = build_workload(args.workload, rank, device)
+    step = wl["step"]
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    if args.no_graph:
+        warm = lambda: [step(i) for i in range(args.warmup)]
+        timed = lambda: [step(args.warmup + i) for i in range(args.steps)]
+    else:
+        gw = capture(step, args.warmup, 0)
+        gt = capture(step, args.steps, args.warmup)
+        warm, timed = gw.replay, gt.replay
+    # sustained load with clock sampling, then the warm-up steps
+    sampler.start()
+    t_end = time.perf_counter() + args.clock_window
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            warm()
+        torch.cuda.synchronize()
+    warm()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    timed()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    per_step_s = ms_max / 1e3 / args.steps
+    value = world * wl["bytes"] / per_step_s / 1e9
+
+    # dominant kernel alone, back to back on the same stream
+    dom = wl["dominant"]
+    if wl["launches"] == 1:
+        dom_s = per_step_s
+    else:
+        gd = capture(dom, args.steps, args.warmup) if not args.no_graph else None
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        gd.replay() if gd is not None else [dom(args.warmup + i) for i in range(args.steps)]
+        d1.record(stream)
+        torch.cuda.synchronize()
+        dom_s = d0.elapsed_time(d1) / 1e3 / args.steps
+    peak, peak_kind = peaks()
+    achieved = wl["dominant_bytes"] / dom_s / 1e9
+    traffic = ncu_traffic(args.workload)
+
+    e2e = None
+    if wl["e2e"] is not None:
+        dt, hb, db = e2e_dropin(args, wl["e2e"], local)
+        if world > 1:
+            tt = torch.tensor([dt], device=device, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            dt = float(tt.item())
+        e2e = {"value": round(world * wl["bytes"] / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": hb,
+               "d2h_bytes_per_step": db, "us_per_step": round(dt * 1e6, 2),
+               "path": "writeBuffer + execute + readBuffer (reference ABI, synchronous, host wall clock)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_baseline(args.workload)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": f"{WORKLOADS[args.workload]} achieved HBM GB/s",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_step_s * 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "description": WORKLOADS[args.workload],
+                       "bytes_per_step": wl["bytes"], "per_rank": wl["meta"],
+                       "l2": "rotating weight pool >= 4x L2; each step reads weights last touched a full pool ago",
+                       "graph": not args.no_graph, "pdl": not args.no_pdl,
+                       "parallelism": f"row shards x{world}, no collective" if world > 1 else "1 GPU"},
+            "frac_of_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": wl["dominant_name"], "achieved": round(achieved, 2),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "algorithmic_bytes": wl["dominant_bytes"],
+                         "us_per_launch": round(dom_s * 1e6, 3)},
+            "gpu_launches": args.steps * wl["launches"],
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,119 @@
+/*
+ * vk_compute_b200.h -- native C ABI of libvkcompute (sm_100a).
+ *
+ * Device pointers, plain sizes and a CUDA stream passed as void* (NULL = the
+ * legacy default stream).  Every function returns 0 on success or a negative
+ * status (VKC_ERR_*) with a message in vkc_last_error(); no function exits
+ * the process.  Kernels are enqueued asynchronously on `stream`.
+ *
+ * Weight arguments use vk-compute's storage exactly:
+ *   bits 32 / 16 / 8 / 4 -- fp32, fp16, u8 codes or u4 codes
+ *   w      -- the transpose_block16 layout (src/data.c:198-222): chunk row r
+ *             holds k in [r*128/bits, (r+1)*128/bits) of column j as 16 bytes
+ *             at byte (r*N + j)*16; 16-byte aligned
+ *   scale, zero -- fp32, [N/256][K] block-major (src/data.c:122-124);
+ *             quantised weights dequantise as q*scale - zero; NULL for
+ *             fp32/fp16 weights
+ *   x, gamma -- fp32 [K]; y -- fp32 [N]
+ * Each function names the reference shader whose computation it replaces
+ * (paths relative to the vk-compute project root).
+ */
+#ifndef VK_COMPUTE_B200_H
+#define VK_COMPUTE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VKC_VERSION 1
+
+#define VKC_OK 0
+#define VKC_ERR_ARG (-1)
+#define VKC_ERR_CUDA (-2)
+#define VKC_ERR_UNSUPPORTED (-3)
+#define VKC_ERR_TIMEOUT (-4)
+
+/* Message of the last failed call on this thread. */
+const char* vkc_last_error(void);
+int vkc_version(void);
+/* Launch later kernels with programmatic dependent launch (1) or plainly (0):
+ * a kernel may then start streaming weights while its predecessor in the
+ * stream finishes; activations are read only after the predecessor's writes
+ * are visible. */
+void vkc_set_pdl(int enable);
+int vkc_get_pdl(void);
+/* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
+int vkc_has_operator(const char* shader);
+
+/* y = W^T x.  Replaces shader/GEMV-FP16.comp, GEMV-INT8.comp, GEMV-INT4.comp
+ * and gemv.comp (fp32), bindings {x, W, y[, s, z]}. */
+int vkc_gemv(int bits, const void* w, const float* scale, const float* zero, const float* x,
+             float* y, int N, int K, void* stream);
+
+/* y = W^T (x * gamma * inv_rms), inv_rms = 1/sqrt(sum(x^2)/rms_dim + eps).
+ * Replaces shader/RmsNorm-GEMV-FP16.comp, -INT8.comp, -INT4.comp and
+ * RmsNorm-GEMV.comp (which fix rms_dim = 4096, eps = 1e-5). */
+int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* zero,
+                     const float* x, const float* gamma, float* y, int N, int K, float eps,
+                     int rms_dim, void* stream);
+
+/* RmsNorm-GEMV followed by a rotary epilogue at position `pos`.
+ * rope_mode 0: the epilogue of shader/RmsNorm-GEMV-Rope-FP16.comp:76-89 as
+ *   written (first 64 outputs of every 256, partner term taken from theta;
+ *   theta holds >= 64 floats).
+ * rope_mode 1: rotation of adjacent pairs (2p, 2p+1) of each head_dim-wide
+ *   head among the first rot_rows outputs by angle pos*theta[p]
+ *   (theta holds >= head_dim/2 floats); rows from rot_rows on (V) unrotated.
+ * Replaces shader/RmsNorm-GEMV-Rope-FP16.comp, -INT8.comp, -INT4.comp. */
+int vkc_rmsnorm_gemv_rope(int bits, const void* w, const float* scale, const float* zero,
+                          const float* x, const float* gamma, const float* theta, float* y,
+                          int N, int K, float eps, int rms_dim, int pos, int rope_mode,
+                          int head_dim, int rot_rows, void* stream);
+
+/* h = SiLU(Wg^T n) * (Wu^T n), n = x * gamma * inv_rms, SiLU(g) =
+ * g / (1 + 2^(-g log2 e)).  Replaces shader/RmsNorm-swiglu-ffn-FP16.comp,
+ * -INT8.comp, -INT4.comp and RmsNorm-swiglu-ffn.comp. */
+int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
+                       const float* su, const float* zu, const float* x, const float* gamma,
+                       float* h, int N, int K, float eps, int rms_dim, void* stream);
+
+/* Decode attention for one token.  Replaces shader/Att-full-FP16.comp.
+ * q: [n_q][head_dim], fp16 (q_bits 16) or fp32 (q_bits 32);
+ * kcache: fp16 K[t][kv][d] at (t*n_kv + kv)*head_dim + d;
+ * vcache: fp16 V[kv][d/8][t][d%8] (16-byte chunks of 8 dims per token);
+ * out: fp32 [n_q][head_dim]; query head h reads KV head h/(n_q/n_kv);
+ * scores are scale * q.k; n_q/n_kv in {1, 2, 4}; head_dim a multiple of 8
+ * up to 256.  workspace: NULL to use a library-owned per-device workspace
+ * (calls on different streams must then not overlap), or caller memory of
+ * vkc_attention_workspace_bytes() bytes, zero-filled before its first use. */
+size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
+int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
+                         float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* C = A B, row-major fp32 (A M x K, B K x N).  Replaces shader/gemm.comp. */
+int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, void* stream);
+
+/* ---- weight preparation on the GPU (bit-identical to src/data.c) ---- */
+
+/* dst[r*N + c] = get_pseudo_random(r, c, seed) (src/data.c:8-28); fp32 when
+ * out_bits = 32, the reference's truncating fp16 (src/data.c:30-51) when 16. */
+int vkc_generate(int seed, int M, int N, int out_bits, void* dst, void* stream);
+/* Quantise a K x N fp32 matrix into the reference's storage: codes (u8 K x N,
+ * or u4 two per byte with the even output in the high nibble) plus block-major
+ * fp32 scale/zero.  symmetric 0: min/max asymmetric (src/data.c:95-185);
+ * symmetric 1: s = max|w|/qmax (fp16-rounded if fp16_scale), u = q + 2^(bits-1),
+ * z = 2^(bits-1) s. */
+int vkc_quantize(const float* w, int K, int N, int bits, int symmetric, int fp16_scale,
+                 uint8_t* codes, float* scale, float* zero, void* stream);
+/* transpose_block16 (src/data.c:198-222) on the device: `in` is K x N
+ * row-major (fp32, fp16, u8, or u4 two per byte). */
+int vkc_pack_block16(const void* in, void* out, int K, int N, int bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

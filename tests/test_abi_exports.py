@@ -1,0 +1,55 @@
+"""libvkcompute.so loads on a machine without a GPU and exports every
+function that include/*.h declares (no compute call is made)."""
+import re
+from pathlib import Path
+
+import pytest
+
+from vk_compute_b200._lib import lib
+
+INCLUDE = Path(__file__).resolve().parents[1] / "include"
+DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([A-Za-z_]\w*)\s*\([^;{]*\)\s*;", re.M)
+
+
+def declared_functions():
+    names = set()
+    for h in INCLUDE.glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"//.*", "", text)
+        for m in DECL.finditer(text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_headers_declare_the_reference_abi():
+    names = set(declared_functions())
+    for fn in ("createSession", "destroySession", "createBuffer", "createTransferAndCopy", "readBuffer",
+               "destroyBuffer", "execute", "getExecutionTime", "createDevice", "destroyDevice",
+               "createPipeline", "destroyPipeline", "createDescriptor", "destroyDescriptor",
+               "createCommand", "destroyCommand", "createFence", "getData", "getDataFP16", "getDataINT8",
+               "getDataINT4", "transpose", "transpose_block16", "free_quantized_data"):
+        assert fn in names, fn
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_symbol_exported(name):
+    assert hasattr(lib(), name), f"libvkcompute.so does not export {name}"
+
+
+REFERENCE_SHADERS = [
+    "GEMV-FP16.spv", "GEMV-INT8.spv", "GEMV-INT4.spv", "GEMV.spv", "RmsNorm-GEMV.spv",
+    "RmsNorm-GEMV-FP16.spv", "RmsNorm-GEMV-INT8.spv", "RmsNorm-GEMV-INT4.spv",
+    "RmsNorm-GEMV-Rope-FP16.spv", "RmsNorm-GEMV-Rope-INT8.spv", "RmsNorm-GEMV-Rope-INT4.spv",
+    "RmsNorm-swiglu-ffn.spv", "RmsNorm-swiglu-ffn-FP16.spv", "RmsNorm-swiglu-ffn-INT8.spv",
+    "RmsNorm-swiglu-ffn-INT4.spv", "Att-full-FP16.spv", "gemm.spv", "bin/GEMV-INT4.spv",
+    "shader\\gemm.comp",
+]
+
+
+@pytest.mark.parametrize("shader", REFERENCE_SHADERS)
+def test_operator_registered(shader):
+    assert lib().vkc_has_operator(shader.encode()) == 1
+
+
+def test_unknown_operator():
+    assert lib().vkc_has_operator(b"RmsNorm-QKV-score-V.spv") == 0

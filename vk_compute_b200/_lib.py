@@ -1,0 +1,61 @@
+"""ctypes binding of libvkcompute.so (the in-tree sm_100a library).
+
+Loading fails loudly when the library has not been built: there is no
+fallback implementation of any operator.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libvkcompute.so"
+
+_lib: C.CDLL | None = None
+
+_i, _f, _p, _sz = C.c_int, C.c_float, C.c_void_p, C.c_size_t
+
+# name -> (restype, argtypes); mirrors include/vk_compute_b200.h
+SIGNATURES = {
+    "vkc_last_error": (C.c_char_p, []),
+    "vkc_version": (_i, []),
+    "vkc_set_pdl": (None, [_i]),
+    "vkc_get_pdl": (_i, []),
+    "vkc_has_operator": (_i, [C.c_char_p]),
+    "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),
+    "vkc_rmsnorm_gemv": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
+    "vkc_rmsnorm_gemv_rope": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p]),
+    "vkc_rmsnorm_swiglu": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
+    "vkc_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "vkc_attention_decode": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
+    "vkc_gemm_f32": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "vkc_generate": (_i, [_i, _i, _i, _i, _p, _p]),
+    "vkc_quantize": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p]),
+    "vkc_pack_block16": (_i, [_p, _p, _i, _i, _i, _p]),
+}
+
+
+class VkcError(RuntimeError):
+    pass
+
+
+def lib() -> C.CDLL:
+    """The loaded library (loaded once, with its argument types declared)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise VkcError(
+                f"{LIB_PATH} is missing: build it with `python -m vk_compute_b200._build` "
+                "(there is no non-CUDA implementation)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        msg = lib().vkc_last_error().decode(errors="replace")
+        raise VkcError(f"libvkcompute error {rc}: {msg}")

@@ -1,0 +1,465 @@
+// Drop-in host runtime: vk-compute's session / buffer / dispatch ABI
+// (include/session.h, buffer.h, dispatch.h, device.h, pipeline.h,
+// descriptor.h, command.h, fence.h) on one CUDA device and stream.
+//
+// The reference records one command buffer per execute() call, binds a
+// freshly built pipeline per operation and waits on a fence
+// (src/dispatch.c:8-61).  Here an operation name selects a compiled sm_100a
+// launcher, its bindings are checked against the sizes the operator will
+// touch, the launches go onto the session stream between two timing events,
+// and execute() returns after the stream drains.  Fatal conditions print to
+// stderr and exit, as every failure path of the reference does
+// (e.g. src/buffer.c:21-32, src/pipeline.c:9-11).
+#include "vkc_common.cuh"
+
+#include <cctype>
+#include <cstdarg>
+#include <cstdlib>
+#include <cstring>
+
+extern "C" {
+#include "session.h"
+#include "buffer.h"
+#include "dispatch.h"
+#include "device.h"
+#include "pipeline.h"
+#include "descriptor.h"
+#include "command.h"
+#include "fence.h"
+#include "vk_compute_b200.h"
+}
+
+namespace vkc {
+
+static thread_local char g_err[512] = "";
+static bool g_pdl = false;
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+bool pdl_enabled() { return g_pdl; }
+
+int launch_attrs(cudaLaunchAttribute* attrs, int cluster_x) {
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = cluster_x < 1 ? 1 : cluster_x;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+    return 2;
+}
+
+namespace {
+
+// Context record behind VkInstance / VkDevice.
+struct Ctx {
+    uint32_t magic;
+    int ordinal;
+    cudaStream_t stream;
+    cudaEvent_t ev_begin, ev_end;
+    bool timed;
+};
+constexpr uint32_t kCtxMagic = 0x564b4331u;  // "VKC1"
+
+[[noreturn]] void fatal(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    fputs("Error: ", stderr);
+    vfprintf(stderr, fmt, ap);
+    fputc('\n', stderr);
+    va_end(ap);
+    exit(EXIT_FAILURE);
+}
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fatal("%s failed: %s", what, cudaGetErrorString(e));
+}
+
+Ctx* ctx_of(const void* handle) {
+    Ctx* c = reinterpret_cast<Ctx*>(const_cast<void*>(handle));
+    if (!c || c->magic != kCtxMagic) fatal("invalid device handle");
+    check_cuda(cudaSetDevice(c->ordinal), "cudaSetDevice");
+    return c;
+}
+
+// ---------------------------------------------------------------------------
+// Operator registry: reference shader name -> launcher
+// ---------------------------------------------------------------------------
+enum OpKind { kOpGemv, kOpRmsGemv, kOpRope, kOpSwiglu, kOpAttention, kOpGemm };
+
+struct OpInfo {
+    const char* name;  // shader base name, without directory or extension
+    OpKind kind;
+    int bits;          // weight width (0 when not applicable)
+};
+
+// Bindings per operator (shader layout(binding = i) declarations):
+//   GEMV-*            {x, W, y [, s, z]}             shader/GEMV-INT8.comp:14-16,68-69
+//   RmsNorm-GEMV-*    {x, gamma, W, y [, s, z]}      shader/RmsNorm-GEMV-INT8.comp:93-98
+//   RmsNorm-GEMV-Rope {x, gamma, W, y, theta}        shader/RmsNorm-GEMV-Rope-FP16.comp:21-25
+//                     {x, gamma, W, y, s, z, theta}  shader/RmsNorm-GEMV-Rope-INT4.comp
+//   swiglu            {x, gamma, G, U, y [, sG, zG, sU, zU]}  shader/RmsNorm-swiglu-ffn-INT4.comp:20-28
+//   Att-full-FP16     {K, V, Q, y}                   shader/Att-full-FP16.comp:21-24
+//   gemm              {A, B, C}                      shader/gemm.comp:12-14
+const OpInfo kOps[] = {
+    {"gemv", kOpGemv, 32},
+    {"gemv-fp32", kOpGemv, 32},
+    {"gemv-fp16", kOpGemv, 16},
+    {"gemv-int8", kOpGemv, 8},
+    {"gemv-int4", kOpGemv, 4},
+    {"rmsnorm-gemv", kOpRmsGemv, 32},
+    {"rmsnorm-gemv-fp16", kOpRmsGemv, 16},
+    {"rmsnorm-gemv-int8", kOpRmsGemv, 8},
+    {"rmsnorm-gemv-int4", kOpRmsGemv, 4},
+    {"rmsnorm-gemv-rope-fp16", kOpRope, 16},
+    {"rmsnorm-gemv-rope-int8", kOpRope, 8},
+    {"rmsnorm-gemv-rope-int4", kOpRope, 4},
+    {"rmsnorm-swiglu-ffn", kOpSwiglu, 32},
+    {"rmsnorm-swiglu-ffn-fp16", kOpSwiglu, 16},
+    {"rmsnorm-swiglu-ffn-int8", kOpSwiglu, 8},
+    {"rmsnorm-swiglu-ffn-int4", kOpSwiglu, 4},
+    {"att-full-fp16", kOpAttention, 16},
+    {"gemm", kOpGemm, 32},
+};
+
+const OpInfo* find_op(const char* shader) {
+    const char* base = shader;
+    for (const char* p = shader; *p; ++p)
+        if (*p == '/' || *p == '\\') base = p + 1;
+    char key[128];
+    size_t n = 0;
+    for (; base[n] && n + 1 < sizeof key; ++n) key[n] = static_cast<char>(tolower(base[n]));
+    key[n] = '\0';
+    const size_t len = strlen(key);
+    if (len > 4 && strcmp(key + len - 4, ".spv") == 0) key[len - 4] = '\0';
+    if (len > 5 && strcmp(key + len - 5, ".comp") == 0) key[len - 5] = '\0';
+    for (const OpInfo& op : kOps)
+        if (strcmp(op.name, key) == 0) return &op;
+    return nullptr;
+}
+
+// The reference shaders' compile-time constants.
+constexpr float kRefEps = 1e-5f;   // shader/RmsNorm-GEMV-FP16.comp:18
+constexpr int kRefDModel = 4096;   // shader/RmsNorm-GEMV-FP16.comp:8
+
+void need_bytes(const operation& op, int idx, int64_t bytes, const char* what) {
+    if (op.buffers[idx].buffer == nullptr) fatal("%s: binding %d (%s) is empty", op.shader, idx, what);
+    if (op.buffers[idx].size < bytes)
+        fatal("%s: binding %d (%s) holds %lld bytes, needs %lld", op.shader, idx, what,
+              static_cast<long long>(op.buffers[idx].size), static_cast<long long>(bytes));
+}
+
+const void* dptr(const operation& op, int idx) { return op.buffers[idx].buffer; }
+
+void run_op(Ctx* c, const operation& op) {
+    const OpInfo* info = find_op(op.shader);
+    if (!info) fatal("unknown operator (shader) name: %s", op.shader);
+    if (op.pushConstantCount < 3 || op.pushConstantCount > MAX_PUSH_CONSTANTS)
+        fatal("%s: expected at least 3 push constants {M, N, K}, got %d", op.shader,
+              op.pushConstantCount);
+    const int N = op.pushConstants[1];
+    const int K = op.pushConstants[2];
+    const int bits = info->bits;
+    if (N <= 0 || K <= 0) fatal("%s: N=%d and K=%d must be positive", op.shader, N, K);
+    const int64_t wbytes = static_cast<int64_t>(K) * N * bits / 8;
+    const int64_t sz_bytes = static_cast<int64_t>(K) * (N / 256) * 4;
+    const bool quant = bits <= 8;
+    int rc = 0;
+    auto need_count = [&](int n) {
+        if (op.bufferCount < n) fatal("%s: expects %d bindings, got %d", op.shader, n, op.bufferCount);
+    };
+    switch (info->kind) {
+        case kOpGemv: {
+            need_count(quant ? 5 : 3);
+            need_bytes(op, 0, 4LL * K, "x");
+            need_bytes(op, 1, wbytes, "W");
+            need_bytes(op, 2, 4LL * N, "y");
+            if (quant) {
+                need_bytes(op, 3, sz_bytes, "scale");
+                need_bytes(op, 4, sz_bytes, "zero");
+            }
+            rc = vkc_gemv(bits, dptr(op, 1), quant ? (const float*)dptr(op, 3) : nullptr,
+                          quant ? (const float*)dptr(op, 4) : nullptr, (const float*)dptr(op, 0),
+                          (float*)dptr(op, 2), N, K, c->stream);
+            break;
+        }
+        case kOpRmsGemv: {
+            need_count(quant ? 6 : 4);
+            need_bytes(op, 0, 4LL * K, "x");
+            need_bytes(op, 1, 4LL * K, "gamma");
+            need_bytes(op, 2, wbytes, "W");
+            need_bytes(op, 3, 4LL * N, "y");
+            if (quant) {
+                need_bytes(op, 4, sz_bytes, "scale");
+                need_bytes(op, 5, sz_bytes, "zero");
+            }
+            rc = vkc_rmsnorm_gemv(bits, dptr(op, 2), quant ? (const float*)dptr(op, 4) : nullptr,
+                                  quant ? (const float*)dptr(op, 5) : nullptr,
+                                  (const float*)dptr(op, 0), (const float*)dptr(op, 1),
+                                  (float*)dptr(op, 3), N, K, kRefEps, kRefDModel, c->stream);
+            break;
+        }
+        case kOpRope: {
+            if (op.pushConstantCount < 4)
+                fatal("%s: expected push constants {M, N, K, tokenIdx}", op.shader);
+            const int tb = quant ? 6 : 4;  // theta binding
+            need_count(tb + 1);
+            need_bytes(op, 0, 4LL * K, "x");
+            need_bytes(op, 1, 4LL * K, "gamma");
+            need_bytes(op, 2, wbytes, "W");
+            need_bytes(op, 3, 4LL * N, "y");
+            if (quant) {
+                need_bytes(op, 4, sz_bytes, "scale");
+                need_bytes(op, 5, sz_bytes, "zero");
+            }
+            // {M, N, K, tokenIdx} selects the reference epilogue; a fifth and
+            // sixth push constant {head_dim, rotated rows} select rotary
+            // embedding on adjacent pairs of each head.
+            int mode = 0, hd = 0, rot = 0;
+            if (op.pushConstantCount >= 6 && op.pushConstants[4] > 0) {
+                mode = 1;
+                hd = op.pushConstants[4];
+                rot = op.pushConstants[5];
+                need_bytes(op, tb, 4LL * (hd / 2), "theta");
+            } else {
+                need_bytes(op, tb, 4LL * 64, "theta");
+            }
+            rc = vkc_rmsnorm_gemv_rope(bits, dptr(op, 2), quant ? (const float*)dptr(op, 4) : nullptr,
+                                       quant ? (const float*)dptr(op, 5) : nullptr,
+                                       (const float*)dptr(op, 0), (const float*)dptr(op, 1),
+                                       (const float*)dptr(op, tb), (float*)dptr(op, 3), N, K,
+                                       kRefEps, kRefDModel, op.pushConstants[3], mode, hd, rot,
+                                       c->stream);
+            break;
+        }
+        case kOpSwiglu: {
+            need_count(quant ? 9 : 5);
+            need_bytes(op, 0, 4LL * K, "x");
+            need_bytes(op, 1, 4LL * K, "gamma");
+            need_bytes(op, 2, wbytes, "gate W");
+            need_bytes(op, 3, wbytes, "up W");
+            need_bytes(op, 4, 4LL * N, "y");
+            if (quant)
+                for (int i = 5; i < 9; ++i) need_bytes(op, i, sz_bytes, "scale/zero");
+            rc = vkc_rmsnorm_swiglu(
+                bits, dptr(op, 2), quant ? (const float*)dptr(op, 5) : nullptr,
+                quant ? (const float*)dptr(op, 6) : nullptr, dptr(op, 3),
+                quant ? (const float*)dptr(op, 7) : nullptr, quant ? (const float*)dptr(op, 8) : nullptr,
+                (const float*)dptr(op, 0), (const float*)dptr(op, 1), (float*)dptr(op, 4), N, K,
+                kRefEps, kRefDModel, c->stream);
+            break;
+        }
+        case kOpAttention: {
+            // {M, N, K, context_length [, head_dim, n_kv_heads, scale bits]}:
+            // N = query heads x head_dim; head_dim defaults to the shader's 256
+            // (shader/Att-full-FP16.comp:8), KV heads to N/head_dim/4 (the
+            // shader's q_head/4, comp:34) and the score scale to 1 (comp:66).
+            if (op.pushConstantCount < 4)
+                fatal("%s: expected push constants {M, N, K, context_length}", op.shader);
+            need_count(4);
+            const int pc_n = op.pushConstantCount;
+            const int hd = pc_n >= 5 && op.pushConstants[4] > 0 ? op.pushConstants[4] : 256;
+            if (N % hd != 0) fatal("%s: N=%d is not a multiple of head_dim %d", op.shader, N, hd);
+            const int n_q = N / hd;
+            int n_kv = pc_n >= 6 && op.pushConstants[5] > 0 ? op.pushConstants[5] : n_q / 4;
+            if (n_kv <= 0 || n_q % n_kv != 0)
+                fatal("%s: %d query heads cannot share %d KV heads", op.shader, n_q, n_kv);
+            float scale = 1.0f;
+            if (pc_n >= 7 && op.pushConstants[6] != 0) memcpy(&scale, &op.pushConstants[6], 4);
+            const int ctxlen = op.pushConstants[3];
+            if (ctxlen <= 0) fatal("%s: context_length=%d must be positive", op.shader, ctxlen);
+            const int64_t kvbytes = 2LL * ctxlen * n_kv * hd;
+            need_bytes(op, 0, kvbytes, "K cache");
+            need_bytes(op, 1, kvbytes, "V cache");
+            need_bytes(op, 2, 2LL * N, "q");
+            need_bytes(op, 3, 4LL * N, "y");
+            rc = vkc_attention_decode(dptr(op, 2), 16, dptr(op, 0), dptr(op, 1), (float*)dptr(op, 3),
+                                      n_q, n_kv, hd, ctxlen, scale, nullptr, 0, c->stream);
+            break;
+        }
+        case kOpGemm: {
+            need_count(3);
+            const int M = op.pushConstants[0];
+            if (M <= 0) fatal("%s: M=%d must be positive", op.shader, M);
+            need_bytes(op, 0, 4LL * M * K, "A");
+            need_bytes(op, 1, 4LL * K * N, "B");
+            need_bytes(op, 2, 4LL * M * N, "C");
+            rc = vkc_gemm_f32((const float*)dptr(op, 0), (const float*)dptr(op, 1),
+                              (float*)dptr(op, 2), M, N, K, c->stream);
+            break;
+        }
+    }
+    if (rc != 0) fatal("%s: %s", op.shader, vkc_last_error());
+}
+
+}  // namespace
+}  // namespace vkc
+
+using namespace vkc;
+
+extern "C" {
+
+const char* vkc_last_error(void) { return g_err; }
+void vkc_set_pdl(int enable) { g_pdl = enable != 0; }
+int vkc_get_pdl(void) { return g_pdl ? 1 : 0; }
+int vkc_version(void) { return VKC_VERSION; }
+
+// --- device.h --------------------------------------------------------------
+device createDevice() {
+    int ordinal = 0;
+    if (const char* env = getenv("VKC_DEVICE")) ordinal = atoi(env);
+    int count = 0;
+    check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (count == 0) fatal("no CUDA device found");
+    if (ordinal < 0 || ordinal >= count) fatal("VKC_DEVICE=%d out of range (%d devices)", ordinal, count);
+    check_cuda(cudaSetDevice(ordinal), "cudaSetDevice");
+    Ctx* c = new Ctx();
+    c->magic = kCtxMagic;
+    c->ordinal = ordinal;
+    check_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    check_cuda(cudaEventCreate(&c->ev_begin), "cudaEventCreate");
+    check_cuda(cudaEventCreate(&c->ev_end), "cudaEventCreate");
+    c->timed = false;
+    device d;
+    d.instance = reinterpret_cast<VkInstance>(c);
+    d.device = reinterpret_cast<VkDevice>(c);
+    d.queue = reinterpret_cast<VkQueue>(c->stream);
+    d.physicalDevice = reinterpret_cast<VkPhysicalDevice>(static_cast<intptr_t>(ordinal + 1));
+    return d;
+}
+
+void destroyDevice(device dev) {
+    Ctx* c = ctx_of(dev.device);
+    cudaStreamSynchronize(c->stream);
+    cudaEventDestroy(c->ev_begin);
+    cudaEventDestroy(c->ev_end);
+    cudaStreamDestroy(c->stream);
+    c->magic = 0;
+    delete c;
+}
+
+// --- session.h -------------------------------------------------------------
+session createSession() {
+    session s;
+    memset(&s, 0, sizeof s);
+    s.dev = createDevice();
+    s.qpool = reinterpret_cast<VkQueryPool>(s.dev.device);
+    return s;
+}
+
+void destroySession(session s) { destroyDevice(s.dev); }
+
+// --- buffer.h --------------------------------------------------------------
+buffer createBuffer(VkDevice dev, VkPhysicalDevice, void* data, int64_t size, int memoryType) {
+    Ctx* c = ctx_of(dev);
+    if (size < 0) fatal("createBuffer: negative size %lld", static_cast<long long>(size));
+    if (memoryType != MEMORY_RAM && memoryType != MEMORY_VRAM)
+        fatal("createBuffer: unknown memory type %d", memoryType);
+    buffer b;
+    memset(&b, 0, sizeof b);
+    const size_t alloc = (static_cast<size_t>(size) + 255) & ~static_cast<size_t>(255);
+    void* p = nullptr;
+    if (cudaMalloc(&p, alloc ? alloc : 256) != cudaSuccess)
+        fatal("Failed to allocate memory! (%lld bytes)", static_cast<long long>(size));
+    if (data && size > 0)
+        check_cuda(cudaMemcpyAsync(p, data, static_cast<size_t>(size), cudaMemcpyHostToDevice, c->stream),
+                   "cudaMemcpyAsync");
+    else
+        check_cuda(cudaMemsetAsync(p, 0, alloc ? alloc : 256, c->stream), "cudaMemsetAsync");
+    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    b.buffer = reinterpret_cast<VkBuffer>(p);
+    b.memory = reinterpret_cast<VkDeviceMemory>(p);
+    b.memReqs.size = alloc;
+    b.memReqs.alignment = 256;
+    b.memReqs.memoryTypeBits = 1u << memoryType;
+    b.size = size;
+    b.memoryType = memoryType;
+    return b;
+}
+
+void createTransferAndCopy(VkDevice dev, VkQueue, buffer*, int) {
+    Ctx* c = ctx_of(dev);
+    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+}
+
+void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* output) {
+    Ctx* c = ctx_of(dev);
+    if (!buf.buffer) fatal("readBuffer: empty buffer");
+    if (buf.size > 0)
+        check_cuda(cudaMemcpyAsync(output, buf.buffer, static_cast<size_t>(buf.size),
+                                   cudaMemcpyDeviceToHost, c->stream),
+                   "cudaMemcpyAsync");
+    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+}
+
+void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
+    Ctx* c = ctx_of(dev);
+    if (!buf.buffer) fatal("writeBuffer: empty buffer");
+    if (buf.size > 0)
+        check_cuda(cudaMemcpyAsync(buf.buffer, data, static_cast<size_t>(buf.size),
+                                   cudaMemcpyHostToDevice, c->stream),
+                   "cudaMemcpyAsync");
+    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+}
+
+void destroyBuffer(VkDevice dev, buffer buf) {
+    Ctx* c = ctx_of(dev);
+    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    if (buf.buffer) check_cuda(cudaFree(buf.buffer), "cudaFree");
+}
+
+// --- dispatch.h ------------------------------------------------------------
+void execute(session s, operation ops[], int opCount) {
+    Ctx* c = ctx_of(s.dev.device);
+    if (opCount < 0) fatal("execute: negative operation count");
+    check_cuda(cudaEventRecord(c->ev_begin, c->stream), "cudaEventRecord");
+    for (int i = 0; i < opCount; ++i) run_op(c, ops[i]);
+    check_cuda(cudaEventRecord(c->ev_end, c->stream), "cudaEventRecord");
+    check_cuda(cudaStreamSynchronize(c->stream), "execute");
+    check_cuda(cudaGetLastError(), "execute");
+    c->timed = true;
+}
+
+double getExecutionTime(session s) {
+    Ctx* c = ctx_of(s.dev.device);
+    if (!c->timed) return 0.0;
+    float ms = 0.f;
+    check_cuda(cudaEventElapsedTime(&ms, c->ev_begin, c->ev_end), "cudaEventElapsedTime");
+    return static_cast<double>(ms);
+}
+
+// --- pipeline.h / descriptor.h / command.h / fence.h ----------------------
+pipeline createPipeline(VkDevice, VkDescriptorSetLayout, const char shaderPath[], uint32_t) {
+    if (!find_op(shaderPath)) fatal("Failed to open shader file: %s", shaderPath);
+    pipeline p;
+    memset(&p, 0, sizeof p);
+    return p;
+}
+void destroyPipeline(VkDevice, pipeline) {}
+
+descriptor createDescriptor(VkDevice, int, buffer[]) {
+    descriptor d;
+    memset(&d, 0, sizeof d);
+    return d;
+}
+void destroyDescriptor(VkDevice, descriptor) {}
+
+command createCommand(VkDevice) {
+    command cmd;
+    memset(&cmd, 0, sizeof cmd);
+    return cmd;
+}
+void destroyCommand(VkDevice, command) {}
+
+VkFence createFence(device, command) { return nullptr; }
+
+// Operator lookup for tools and tests: 1 if `shader` names a registered
+// operator, else 0.
+int vkc_has_operator(const char* shader) { return find_op(shader) ? 1 : 0; }
+
+}  // extern "C"

@@ -1,0 +1,191 @@
+"""Torch-facing operators over the C ABI of libvkcompute.
+
+Tensors supply device memory and the current CUDA stream; every operator
+is one call into the sm_100a library (include/vk_compute_b200.h).
+Weights use vk-compute's storage: the 16-byte chunk layout of
+src/data.c:198-222 plus block-major fp32 scale/zero per (k, 256 outputs).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import check, lib
+
+GROUP = 256
+
+
+def _p(t: torch.Tensor | None) -> C.c_void_p | None:
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _s(stream: torch.cuda.Stream | None = None) -> C.c_void_p:
+    s = torch.cuda.current_stream() if stream is None else stream
+    return C.c_void_p(s.cuda_stream)
+
+
+def chunk_elems(bits: int) -> int:
+    """Weights per 16-byte chunk (k values of one output)."""
+    return 128 // bits
+
+
+@dataclass
+class PackedWeight:
+    """One K x N weight matrix (y[j] = sum_k x[k] W[k][j]) in device memory."""
+
+    bits: int
+    K: int
+    N: int
+    packed: torch.Tensor          # uint8, (K / chunk_elems) * N * 16 bytes
+    scale: torch.Tensor | None    # fp32 [N/256 * K], block-major (quantised only)
+    zero: torch.Tensor | None
+
+    @property
+    def nbytes(self) -> int:
+        n = self.packed.numel()
+        if self.scale is not None:
+            n += 4 * (self.scale.numel() + self.zero.numel())
+        return n
+
+    def shard(self, lo: int, hi: int) -> "PackedWeight":
+        """Copy of outputs [lo, hi) (a row shard of W^T).  Chunk rows are
+        contiguous N*16-byte streams, so the shard is a strided gather of
+        (hi-lo)*16 bytes per chunk row; scale/zero blocks are contiguous."""
+        if self.bits <= 8 and (lo % GROUP or hi % GROUP):
+            raise ValueError("quantised shards must be 256-output aligned")
+        R = self.K // chunk_elems(self.bits)
+        p = self.packed.view(R, self.N, 16)[:, lo:hi].contiguous().view(-1)
+        s = z = None
+        if self.scale is not None:
+            s = self.scale.view(self.N // GROUP, self.K)[lo // GROUP:hi // GROUP].contiguous().view(-1)
+            z = self.zero.view(self.N // GROUP, self.K)[lo // GROUP:hi // GROUP].contiguous().view(-1)
+        return PackedWeight(self.bits, self.K, hi - lo, p, s, z)
+
+
+def _alloc_weight(bits: int, K: int, N: int, device) -> PackedWeight:
+    packed = torch.empty(K * N * bits // 8, dtype=torch.uint8, device=device)
+    s = z = None
+    if bits <= 8:
+        s = torch.empty(N // GROUP * K, dtype=torch.float32, device=device)
+        z = torch.empty_like(s)
+    return PackedWeight(bits, K, N, packed, s, z)
+
+
+def pack_dense(w: torch.Tensor, bits: int, symmetric: bool = True, fp16_scale: bool = True,
+               stream=None) -> PackedWeight:
+    """Quantise (bits 8/4) or convert (16/32) a dense K x N matrix on the GPU
+    and pack it.  16-bit weights are rounded to nearest by torch."""
+    K, N = w.shape
+    dev = w.device
+    out = _alloc_weight(bits, K, N, dev)
+    st = _s(stream)
+    if bits in (32, 16):
+        src = w.to(torch.float32 if bits == 32 else torch.float16).contiguous()
+        check(lib().vkc_pack_block16(_p(src), _p(out.packed), K, N, bits, st))
+        return out
+    codes = torch.empty(K * N * bits // 8, dtype=torch.uint8, device=dev)
+    wf = w.to(torch.float32).contiguous()
+    check(lib().vkc_quantize(_p(wf), K, N, bits, int(symmetric), int(fp16_scale), _p(codes),
+                             _p(out.scale), _p(out.zero), st))
+    check(lib().vkc_pack_block16(_p(codes), _p(out.packed), K, N, bits, st))
+    return out
+
+
+def reference_weight(seed: int, K: int, N: int, bits: int, device="cuda", stream=None) -> PackedWeight:
+    """The reference's seeded weights (src/compute.c:20-46): get_pseudo_random
+    values, fp16 by truncation, int8/int4 by the min/max quantiser, packed by
+    transpose_block16 -- all on the GPU, bit-identical to src/data.c."""
+    out = _alloc_weight(bits, K, N, device)
+    st = _s(stream)
+    if bits in (32, 16):
+        raw = torch.empty(K * N, dtype=torch.float32 if bits == 32 else torch.int16, device=device)
+        check(lib().vkc_generate(seed, K, N, bits, _p(raw), st))
+        check(lib().vkc_pack_block16(_p(raw), _p(out.packed), K, N, bits, st))
+        return out
+    vals = torch.empty(K * N, dtype=torch.float32, device=device)
+    check(lib().vkc_generate(seed, K, N, 32, _p(vals), st))
+    codes = torch.empty(K * N * bits // 8, dtype=torch.uint8, device=device)
+    check(lib().vkc_quantize(_p(vals), K, N, bits, 0, 0, _p(codes), _p(out.scale), _p(out.zero), st))
+    check(lib().vkc_pack_block16(_p(codes), _p(out.packed), K, N, bits, st))
+    return out
+
+
+def reference_vector(seed: int, n: int, device="cuda", stream=None) -> torch.Tensor:
+    """getData(seed, 1, n) (src/data.c:18-28) on the GPU."""
+    v = torch.empty(n, dtype=torch.float32, device=device)
+    check(lib().vkc_generate(seed, 1, n, 32, _p(v), _s(stream)))
+    return v
+
+
+def _out(n: int, like: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    if out is None:
+        return torch.empty(n, dtype=torch.float32, device=like.device)
+    return out
+
+
+def gemv(w: PackedWeight, x: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    y = _out(w.N, x, out)
+    check(lib().vkc_gemv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(y), w.N, w.K, _s(stream)))
+    return y
+
+
+def rmsnorm_gemv(w: PackedWeight, x, gamma, eps: float = 1e-6, rms_dim: int | None = None,
+                 out=None, stream=None) -> torch.Tensor:
+    y = _out(w.N, x, out)
+    check(lib().vkc_rmsnorm_gemv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma), _p(y),
+                                 w.N, w.K, eps, rms_dim or w.K, _s(stream)))
+    return y
+
+
+def rmsnorm_gemv_rope(w: PackedWeight, x, gamma, theta, pos: int, *, mode: str = "pairs",
+                      head_dim: int = 128, rot_rows: int | None = None, eps: float = 1e-6,
+                      rms_dim: int | None = None, out=None, stream=None) -> torch.Tensor:
+    y = _out(w.N, x, out)
+    m = {"reference": 0, "pairs": 1}[mode]
+    rot = w.N if rot_rows is None else rot_rows
+    check(lib().vkc_rmsnorm_gemv_rope(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma),
+                                      _p(theta), _p(y), w.N, w.K, eps, rms_dim or w.K, pos, m, head_dim,
+                                      rot, _s(stream)))
+    return y
+
+
+def rmsnorm_swiglu(wg: PackedWeight, wu: PackedWeight, x, gamma, eps: float = 1e-6,
+                   rms_dim: int | None = None, out=None, stream=None) -> torch.Tensor:
+    h = _out(wg.N, x, out)
+    check(lib().vkc_rmsnorm_swiglu(wg.bits, _p(wg.packed), _p(wg.scale), _p(wg.zero), _p(wu.packed),
+                                   _p(wu.scale), _p(wu.zero), _p(x), _p(gamma), _p(h), wg.N, wg.K, eps,
+                                   rms_dim or wg.K, _s(stream)))
+    return h
+
+
+def attention_workspace(n_q: int, n_kv: int, head_dim: int, ctx: int, device="cuda") -> torch.Tensor:
+    n = lib().vkc_attention_workspace_bytes(n_q, n_kv, head_dim, ctx)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def attention_decode(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx: int,
+                     scale: float, workspace: torch.Tensor | None = None, out=None,
+                     stream=None) -> torch.Tensor:
+    """q [n_q*hd] fp16 or fp32; kcache fp16 [ctx][n_kv][hd];
+    vcache fp16 [n_kv][hd/8][ctx][8]."""
+    o = _out(n_q * head_dim, q, out)
+    qb = 32 if q.dtype == torch.float32 else 16
+    ws_n = 0 if workspace is None else workspace.numel()
+    check(lib().vkc_attention_decode(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
+                                     scale, _p(workspace), ws_n, _s(stream)))
+    return o
+
+
+def gemm_f32(a: torch.Tensor, b: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    M, K = a.shape
+    K2, N = b.shape
+    assert K == K2
+    c = torch.empty(M, N, dtype=torch.float32, device=a.device) if out is None else out
+    check(lib().vkc_gemm_f32(_p(a), _p(b), _p(c), M, N, K, _s(stream)))
+    return c
+
+
+def set_pdl(enable: bool) -> None:
+    lib().vkc_set_pdl(int(enable))
