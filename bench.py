@@ -273,7 +273,8 @@ def e2e_dropin(args, e2e, device_index):
         h = t.cpu().numpy()
         return D.create_buffer(s, h)
 
-    bufs = [(dev_buffer(w.packed), dev_buffer(w.scale), dev_buffer(w.zero)) for w in pool[:max(2, len(pool))]]
+    bufs = [(dev_buffer(w.packed), dev_buffer(w.scale) if bits <= 8 else None,
+             dev_buffer(w.zero) if bits <= 8 else None) for w in pool]
     x_host = torch.empty(K, dtype=torch.float32).pin_memory()
     x_host.copy_(x.cpu())
     y_host = torch.empty(N, dtype=torch.float32).pin_memory()
@@ -302,9 +303,10 @@ def e2e_dropin(args, e2e, device_index):
     for i in range(args.steps):
         one(i)
     dt = (time.perf_counter() - t0) / args.steps
-    for wb, sb, zb in bufs:
-        for b in (wb, sb, zb):
-            D.destroy_buffer(s, b)
+    for trio in bufs:
+        for b in trio:
+            if b is not None:
+                D.destroy_buffer(s, b)
     for b in (xb, gb, yb):
         D.destroy_buffer(s, b)
     D.destroy_session(s)

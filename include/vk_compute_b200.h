@@ -47,6 +47,11 @@ void vkc_set_pdl(int enable);
 int vkc_get_pdl(void);
 /* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
 int vkc_has_operator(const char* shader);
+/* Waits for the current device and returns its status word: bit 0 set when a
+ * kernel's producer warp, bit 1 when a consumer warp, gave up a bounded
+ * wait (the kernel then ends early and its outputs are invalid).  `clear`
+ * resets the word.  No counterpart in the reference. */
+int vkc_device_status(unsigned* status, int clear);
 
 /* y = W^T x.  Replaces shader/GEMV-FP16.comp, GEMV-INT8.comp, GEMV-INT4.comp
  * and gemv.comp (fp32), bindings {x, W, y[, s, z]}. */

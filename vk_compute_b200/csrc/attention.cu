@@ -25,13 +25,11 @@
 
 #include <cuda_fp16.h>
 
-#include <mutex>
 
 namespace vkc {
 namespace {
 
 constexpr int kAttThreads = 256;
-constexpr int kMaxGroup = 4;   // query heads per KV head handled per CTA
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnParams {
@@ -248,14 +246,6 @@ __global__ void __launch_bounds__(kAttThreads) attention_decode_kernel(const Att
     if (tid == 0) p.tickets[kv] = 0u;
 }
 
-// Library-owned workspace, one per device, grown on demand.
-struct Workspace {
-    void* ptr = nullptr;
-    size_t bytes = 0;
-};
-std::mutex g_ws_mu;
-Workspace g_ws[64];
-
 }  // namespace
 
 // Splits and tokens per CTA for a context length: about two CTAs per SM.
@@ -329,29 +319,6 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     return kOk;
 }
 
-// Library-owned workspace for `device`: allocated (and its tickets zeroed) on
-// first use and grown when a larger shape arrives.
-int library_workspace(size_t need, void** out, cudaStream_t stream) {
-    int dev = 0;
-    VKC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
-    std::lock_guard<std::mutex> lock(g_ws_mu);
-    Workspace& w = g_ws[dev];
-    if (w.bytes < need) {
-        if (w.ptr) {
-            VKC_CUDA_TRY(cudaStreamSynchronize(stream));
-            VKC_CUDA_TRY(cudaFree(w.ptr));
-            w.ptr = nullptr;
-            w.bytes = 0;
-        }
-        VKC_CUDA_TRY(cudaMalloc(&w.ptr, need));
-        VKC_CUDA_TRY(cudaMemsetAsync(w.ptr, 0, need, stream));
-        w.bytes = need;
-    }
-    *out = w.ptr;
-    return kOk;
-}
-
 }  // namespace vkc
 
 using namespace vkc;
@@ -369,7 +336,9 @@ int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const vo
     if (!workspace) {
         const size_t need = attention_workspace_bytes(n_q > 0 ? n_q : 1, n_kv > 0 ? n_kv : 1,
                                                       head_dim > 0 ? head_dim : 8, ctx > 0 ? ctx : 1);
-        if (int e = library_workspace(need, &workspace, s)) return e;
+        void* base = nullptr;
+        if (int e = device_workspace(need + kWorkspaceHeader, &base, s)) return e;
+        workspace = static_cast<char*>(base) + kWorkspaceHeader;
         workspace_bytes = need;
     }
     return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, scale,

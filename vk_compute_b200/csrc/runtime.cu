@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 extern "C" {
 #include "session.h"
@@ -43,6 +44,39 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 bool pdl_enabled() { return g_pdl; }
+
+namespace {
+struct DeviceScratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+DeviceScratch g_scratch[64];
+}  // namespace
+
+int device_workspace(size_t bytes, void** out, cudaStream_t stream) {
+    int dev = 0;
+    VKC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    DeviceScratch& w = g_scratch[dev];
+    if (w.bytes < bytes) {
+        // Grow to at least 4 MiB so the usual shapes allocate once.
+        size_t want = bytes < (4u << 20) ? (4u << 20) : bytes;
+        if (w.ptr) {
+            VKC_CUDA_TRY(cudaDeviceSynchronize());
+            VKC_CUDA_TRY(cudaFree(w.ptr));
+            w.ptr = nullptr;
+            w.bytes = 0;
+        }
+        VKC_CUDA_TRY(cudaMalloc(&w.ptr, want));
+        VKC_CUDA_TRY(cudaMemsetAsync(w.ptr, 0, want, stream));
+        VKC_CUDA_TRY(cudaStreamSynchronize(stream));
+        w.bytes = want;
+    }
+    *out = w.ptr;
+    return kOk;
+}
 
 int launch_attrs(cudaLaunchAttribute* attrs, int cluster_x) {
     attrs[0].id = cudaLaunchAttributeClusterDimension;

@@ -32,6 +32,14 @@ int set_error(int code, const char* fmt, ...);
 // Programmatic dependent launch switch shared by all launchers.
 bool pdl_enabled();
 
+// Library-owned scratch of the current device: at least `bytes`, zero-filled
+// when (re)allocated.  Kernels that use it leave their ticket words at zero,
+// so consecutive launches on one stream may share it; launches that overlap
+// on different streams must not.  Words [0, 64) are reserved for the status
+// word written by bounded device waits.
+int device_workspace(size_t bytes, void** out, cudaStream_t stream);
+constexpr size_t kWorkspaceHeader = 256;
+
 // Fills the launch attributes every kernel launcher uses: an optional cluster
 // shape (cluster_x > 1) and the programmatic-serialization flag.  Returns the
 // number of attributes written into attrs[0..2).
@@ -80,6 +88,69 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+
+// ---- mbarrier / bulk-copy primitives (Hopper+ async proxy) ----------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on a phase of an mbarrier: false after `limit` polls.
+constexpr uint32_t kSpinLimit = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+// L2 policy for data read exactly once (weights): evict first.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// Global -> shared bulk copy completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).  No multicast.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Status bits a kernel records in the workspace header when a bounded wait
+// gives up.
+enum : uint32_t { kStatusProducerTimeout = 1u, kStatusConsumerTimeout = 2u };
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
