@@ -9,30 +9,30 @@
 // block-major at b*K + k (src/data.c:122-124), dequantised as q*s - z
 // (shader/GEMV-INT8.comp:107).
 //
-// Work decomposition (stream-K).  Outputs form tiles of 256 columns (one
-// scale block); a unit is one chunk row of one tile, a contiguous 4 KB
-// segment.  The tiles x R units, tile-major, are split into equal contiguous
-// ranges over persistent CTAs (two per SM), so every CTA streams the same
-// number of bytes whatever N and K are.  A CTA's range covers whole tiles and
-// at most two partial tiles; a partial tile's contributors write their partial
-// sums to a workspace and the last to finish (atomic ticket) adds them in
-// contributor order and runs the epilogue, so results are deterministic.
+// Decomposition.  A CTA of 256 threads owns C consecutive outputs
+// (C in {256, 128, 64, 32}, inside one scale block) and a range of chunk rows;
+// its 256/C thread groups take interleaved rows.  S CTAs of a thread-block
+// cluster (S <= 8) split K, and their partial sums meet in distributed shared
+// memory, where each rank runs the epilogue for C/S of the outputs.  C and S
+// are chosen so that every CTA has the same work and all CTAs are resident at
+// once (one wave): on a saturated memory system every CTA then streams at the
+// same rate and they finish together.
 //
-// Pipeline.  One producer warp streams each stage -- up to 16 KB of weight
-// rows plus the stage's slice of x, gamma, scale and zero -- into a ring of
-// shared-memory slots with cp.async.bulk completing on mbarriers; the weight
-// copies of the first ring's worth of stages are issued before
-// griddepcontrol.wait, so under programmatic dependent launch they overlap the
-// previous kernel.  Eight consumer warps own one column each per lane.
+// Streaming.  Every thread keeps its own ring of D 16-byte cp.async copies in
+// shared memory (one commit group per row), so D rows per thread are in
+// flight without registers and without any barrier in the steady state; a
+// warp reads 512 contiguous bytes per row.  The few activation loads are
+// issued before the first weight copy, so they are not queued behind the
+// weight stream.
 //
-// Arithmetic.  Per stage the consumers fold the per-(k, b) scale into the
-// activation, x'_k = x_k * gamma_k * s_kb, and accumulate the zero-point term
-// c_b = sum_k x_k gamma_k z_kb and sum x^2, so
-// y_j = inv_rms * (sum_k x'_k q_kj - c_b): one conversion and one fused
-// multiply-add per weight.  Codes become floats exactly by OR-ing them into the
-// mantissa of 2^23 and subtracting 2^23 (int4 nibbles keep their bit position;
-// x' carries the matching power of two); pairs of weights use the packed
-// f32x2 add and FMA.
+// Arithmetic.  The per-(k, b) scale is folded into the staged activation,
+// x'_k = x_k * gamma_k * s_kb, and the zero point into a per-block constant
+// c_b = sum_k x_k gamma_k z_kb, so y_j = inv_rms * (sum_k x'_k q_kj - c_b):
+// one conversion and one fused multiply-add per weight.  Codes become floats
+// exactly by OR-ing them into the mantissa of 2^23 and subtracting 2^23 (int4
+// nibbles keep their bit position; x' carries the matching power of two);
+// pairs of weights use the packed f32x2 add and FMA.  inv_rms and c_b are
+// scalars applied in the epilogue, after the cluster reduction.
 #include "vkc_common.cuh"
 
 #include <cuda_fp16.h>
@@ -40,17 +40,16 @@
 #include <mutex>
 
 namespace vkc {
+
+// Per-device status word (one instance per device context), bits kStatus*.
+__device__ uint32_t g_status = 0;
+
 namespace {
 
-constexpr int kCols = 256;             // outputs per tile (one scale group)
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = 32 * kConsumerWarps;
-constexpr int kThreads = kConsumers + 32;  // + one producer warp
-constexpr int kCtasPerSm = 2;
-constexpr int kStageWeightBytes = 16384;   // weight bytes per pipeline stage
-constexpr int kStages = 5;                 // ring depth
-constexpr int kBarBytes = 128;             // mbarrier block at the start of smem
-constexpr uint32_t kConsumerBar = 1;       // named barrier id of the consumer warps
+constexpr int kThreads = 256;
+constexpr int kGroup = 256;     // outputs per scale block
+constexpr int kCtasPerSm = 4;   // occupancy target (64 registers per thread)
+constexpr int kRingBytes = 32768;  // cp.async ring per CTA (all streams)
 
 enum Mode : int {
     kGemv = 0,       // shader/GEMV-*.comp
@@ -68,56 +67,25 @@ struct GemvParams {
     const float* gamma;
     const float* theta;
     float* y;
-    int N, K, R, tiles;
-    int max_slots;
+    int N, K, R;
+    int cols;      // C: outputs per CTA
+    int rows_cta;  // chunk rows per CTA (the last rank of a cluster may have fewer)
+    int rbuf_floats;  // rank-0 receive buffer, S * (NS*C + 4) floats
     float eps;
     float inv_dim;  // 1 / RMS divisor
     int pos;
     int head_dim;
     int rot_rows;
-    uint32_t* status;   // workspace header word
-    uint32_t* tickets;  // [tiles]
-    float* partial;     // [tiles][max_slots][NS*kCols + 4]
 };
 
-template <int BITS, int NS>
-struct Geometry {
-    static constexpr int KPC = 128 / BITS;                       // k per chunk
-    static constexpr int SR = kStageWeightBytes / (NS * kCols * 16);  // chunk rows per stage
-    static constexpr int SA = SR * KPC;                           // activations per stage
-    static constexpr int kActArrays = 2 + 3 * NS;                 // x, gamma, s[NS], z[NS], x'[NS]
-    static constexpr int kSlotBytes = ((NS * SR * kCols * 16 + SA * 4 * kActArrays) + 127) / 128 * 128;
-    static constexpr int kSmemBytes = kBarBytes + kStages * kSlotBytes;
-    // Offsets inside a slot.
-    static constexpr int kOffX = NS * SR * kCols * 16;
-    static constexpr int kOffGamma = kOffX + SA * 4;
-    static constexpr int kOffS = kOffGamma + SA * 4;
-    static constexpr int kOffZ = kOffS + NS * SA * 4;
-    static constexpr int kOffXp = kOffZ + NS * SA * 4;
-};
-
-// CTA owning unit u when T units are split into P equal contiguous ranges
-// [floor(c*T/P), floor((c+1)*T/P)).
-__host__ __device__ __forceinline__ int cta_of(long long u, long long T, int P) {
-    return static_cast<int>(((u + 1) * P - 1) / T);
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-
-// Walks a CTA's unit range in pipeline stages that never cross a tile.
-struct StageWalk {
-    long long u, u1;
-    int R, SR;
-    __device__ bool next(int& t, int& r, int& nr) {
-        if (u >= u1) return false;
-        t = static_cast<int>(u / R);
-        r = static_cast<int>(u % R);
-        long long n = SR;
-        if (n > R - r) n = R - r;
-        if (n > u1 - u) n = u1 - u;
-        nr = static_cast<int>(n);
-        u += n;
-        return true;
-    }
-};
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Power-of-two pre-scale of an int4 position inside a 32-bit word.  Nibbles
 // 0-4 are decoded in place (bit offsets 0..16); nibbles 5-7 after a 12-bit
@@ -189,27 +157,27 @@ __device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict
 }
 
 // Epilogue for one output column: RMS scale, zero-point constant and the
-// operator's activation.  Called by all consumer threads of a warp together.
+// operator's activation.  Called by every lane of a warp together (the RoPE
+// partner is the neighbouring lane); `active` lanes store.
 template <int MODE, int NS, bool kQuant, bool kNorm>
-__device__ __forceinline__ void finalize(const GemvParams& p, int t, int col, const float (&acc)[NS],
+__device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active, const float (&acc)[NS],
                                          const float (&tot)[3]) {
     float v[NS];
     const float inv = kNorm ? 1.0f / sqrtf(tot[0] * p.inv_dim + p.eps) : 1.0f;
 #pragma unroll
     for (int st = 0; st < NS; ++st) v[st] = ((kQuant ? acc[st] - tot[1 + st] : acc[st])) * inv;
-    const int j = t * kCols + col;
     float out = v[0];
     if constexpr (MODE == kRopeRef) {
         // shader/RmsNorm-GEMV-Rope-FP16.comp:76-89, reproduced as written.
-        const int c = j % kCols;
-        if (c < 64) {
+        const int c = j % kGroup;
+        if (active && c < 64) {
             float sa, ca;
             sincosf(static_cast<float>(p.pos) * p.theta[c / 2], &sa, &ca);
             out = (c & 1) == 0 ? out * ca - p.theta[c + 1] * sa : p.theta[c - 1] * sa + out * ca;
         }
     } else if constexpr (MODE == kRopePairs) {
         const float partner = __shfl_xor_sync(0xffffffffu, out, 1);
-        if (j < p.rot_rows) {
+        if (active && j < p.rot_rows) {
             float sa, ca;
             sincosf(static_cast<float>(p.pos) * p.theta[(j % p.head_dim) >> 1], &sa, &ca);
             out = (j & 1) == 0 ? out * ca - partner * sa : partner * sa + out * ca;
@@ -218,229 +186,223 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int t, int col, co
         // shader/RmsNorm-swiglu-ffn-FP16.comp:86-87
         out = out / (1.0f + exp2f(-out * 1.44269504f)) * v[1];
     }
-    if (j < p.N) p.y[j] = out;
+    if (active && j < p.N) p.y[j] = out;
 }
 
 template <int BITS, int MODE>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvParams p) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
-    using G = Geometry<BITS, NS>;
-    constexpr int KPC = G::KPC, SR = G::SR, SA = G::SA;
+    constexpr int KPC = 128 / BITS;
+    constexpr int D = kRingBytes / (NS * kThreads * 16);  // rows in flight per thread
     constexpr bool kQuant = BITS <= 8;
     constexpr bool kNorm = MODE != kGemv;
 
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[kConsumerWarps][3];
-    __shared__ int s_last;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* ring = reinterpret_cast<uint4*>(smem);                         // [NS][D][256]
+    float* rbuf = reinterpret_cast<float*>(smem + kRingBytes);             // [S][NS*C + 4] (rank 0)
+    float* xs = rbuf + p.rbuf_floats;                                      // [rows_cta][NS][KPC]
+    __shared__ float red[NS][kThreads];                                    // row-group partials
+    __shared__ float wred[kThreads / 32][3];
+    __shared__ __align__(8) uint64_t red_bar;                              // S-1 deposits (rank 0)
 
-    const uint32_t bar0 = smem_addr(smem);
-    auto full_bar = [&](int i) { return bar0 + 8u * i; };
-    auto empty_bar = [&](int i) { return bar0 + 8u * (kStages + i); };
-    uint8_t* slots = smem + kBarBytes;
-
+    uint32_t nctarank, ctarank;
+    asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(nctarank));
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(ctarank));
+    const int S = static_cast<int>(nctarank);
+    const int rank = static_cast<int>(ctarank);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int P = gridDim.x, cta = blockIdx.x;
-    const long long T = static_cast<long long>(p.tiles) * p.R;
-    const long long u0 = cta * T / P, u1 = (cta + 1) * T / P;
+    const int C = p.cols, G = kThreads / C;
+    const int c = tid % C, grp = tid / C;
+    const int col0 = blockIdx.y * C;
+    const int col = col0 + c;
+    const bool col_ok = col < p.N;
+    const int r0 = rank * p.rows_cta;
+    const int nrows = max(0, min(p.rows_cta, p.R - r0));
+    const int nk = nrows * KPC;
+    const size_t sblk = static_cast<size_t>(col0 / kGroup) * p.K;
 
-    if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(full_bar(i), 1);
-            mbar_init(empty_bar(i), kConsumerWarps);
+    if (S > 1) {
+        if (rank == 0 && threadIdx.x == 0) {
+            mbar_init(smem_addr(&red_bar), static_cast<uint32_t>(S - 1));
+            mbar_init_fence();
         }
-        mbar_init_fence();
+        // Rank 0's barrier is initialised before any rank deposits (the
+        // matching wait comes just before the deposits).
+        cluster_arrive_release();
     }
-    __syncthreads();
     pdl_launch_dependents();
 
-    if (warp == kConsumerWarps) {
-        // ------------------------------ producer ------------------------------
-        if (lane != 0) return;
-        const uint64_t pol = l2_evict_first();
-        auto stage_bytes = [&](int t, int nr) -> uint32_t {
-            const int ncols = min(kCols, p.N - t * kCols);
-            return static_cast<uint32_t>(NS * nr * ncols * 16 +
-                                         nr * KPC * 4 * (1 + (kNorm ? 1 : 0) + (kQuant ? 2 * NS : 0)));
-        };
-        auto copy_weights = [&](int slot, int t, int r, int nr) {
-            const int ncols = min(kCols, p.N - t * kCols);
-            const uint32_t dst = smem_addr(slots + slot * G::kSlotBytes);
+    // ---- activations first (gamma / scale / zero, then x after the wait), in
+    // passes of 1024 values held in registers; the first pass is issued before
+    // the weight stream so it is not queued behind it.
+    constexpr int kMaxAct = 4;  // values per thread per pass
+    float av_g[kMaxAct], av_s[NS][kMaxAct], av_z[NS][kMaxAct], av_x[kMaxAct];
+    auto load_acts = [&](int base) {
 #pragma unroll
-            for (int st = 0; st < NS; ++st)
-                for (int i = 0; i < nr; ++i)
-                    bulk_g2s(dst + static_cast<uint32_t>((st * SR + i) * kCols * 16),
-                             p.w[st] + (static_cast<size_t>(r + i) * p.N + static_cast<size_t>(t) * kCols) * 16,
-                             static_cast<uint32_t>(ncols * 16), full_bar(slot), pol);
-        };
-        auto copy_acts = [&](int slot, int t, int r, int nr) {
-            const uint32_t base = smem_addr(slots + slot * G::kSlotBytes);
-            const size_t k0 = static_cast<size_t>(r) * KPC;
-            const uint32_t n = static_cast<uint32_t>(nr * KPC * 4);
-            bulk_g2s(base + G::kOffX, p.x + k0, n, full_bar(slot));
-            if (kNorm) bulk_g2s(base + G::kOffGamma, p.gamma + k0, n, full_bar(slot));
-            if (kQuant) {
-                const size_t sb = static_cast<size_t>(t) * p.K + k0;
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int e = base + tid + q * kThreads;
+            const int k = r0 * KPC + e;
+            const bool ok = e < nk;
+            av_g[q] = (kNorm && ok) ? __ldg(p.gamma + k) : 1.f;
+#pragma unroll
+            for (int st = 0; st < NS; ++st) {
+                av_s[st][q] = (kQuant && ok) ? __ldg(p.s[st] + sblk + k) : 1.f;
+                av_z[st][q] = (kQuant && ok) ? __ldg(p.z[st] + sblk + k) : 0.f;
+            }
+        }
+    };
+    auto load_x = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int e = base + tid + q * kThreads;
+            av_x[q] = e < nk ? p.x[r0 * KPC + e] : 0.f;
+        }
+    };
+    float ss = 0.f, cz[NS];
+#pragma unroll
+    for (int st = 0; st < NS; ++st) cz[st] = 0.f;
+    auto fold = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int e = base + tid + q * kThreads;
+            if (e < nk) {
+                const float xv = av_x[q];
+                float xg = xv;
+                if constexpr (kNorm) {
+                    ss = fmaf(xv, xv, ss);
+                    xg = xv * av_g[q];
+                }
+                const int rl = e / KPC, i = e % KPC;
 #pragma unroll
                 for (int st = 0; st < NS; ++st) {
-                    bulk_g2s(base + G::kOffS + st * SA * 4, p.s[st] + sb, n, full_bar(slot));
-                    bulk_g2s(base + G::kOffZ + st * SA * 4, p.z[st] + sb, n, full_bar(slot));
+                    float v = xg;
+                    if constexpr (kQuant) {
+                        v = xg * av_s[st][q];
+                        cz[st] = fmaf(xg, av_z[st][q], cz[st]);
+                    }
+                    if constexpr (BITS == 4) v *= int4_prescale(i);
+                    xs[(rl * NS + st) * KPC + i] = v;
                 }
             }
-        };
-        StageWalk walk{u0, u1, p.R, SR};
-        StageWalk acts = walk;
-        int t, r, nr, g = 0;
-        // Weights of the first ring's worth of stages do not depend on the
-        // previous kernel: issue them before waiting for it.
-        while (g < kStages && walk.next(t, r, nr)) {
-            mbar_arrive_expect_tx(full_bar(g), stage_bytes(t, nr));
-            copy_weights(g, t, r, nr);
-            ++g;
         }
-        pdl_wait();
-        for (int i = 0; i < g; ++i) {
-            acts.next(t, r, nr);
-            copy_acts(i, t, r, nr);
+    };
+    load_acts(0);
+
+    // ---- weights: prime the ring with D rows per thread ---------------------
+    const int my_rows = nrows > grp ? (nrows - grp + G - 1) / G : 0;  // rows grp, grp+G, ...
+    auto src = [&](int st, int i) {
+        const int r = r0 + grp + i * G;
+        return reinterpret_cast<const uint4*>(p.w[st]) + (static_cast<size_t>(r) * p.N + col);
+    };
+    auto slot = [&](int st, int i) { return smem_addr(ring + (st * D + (i % D)) * kThreads + tid); };
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        if (i < my_rows && col_ok)
+#pragma unroll
+            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i), src(st, i));
+        cp_async_commit();
+    }
+
+    // ---- x depends on the previous kernel: wait for it, then fold --------
+    pdl_wait();
+    load_x(0);
+    fold(0);
+    for (int base = kMaxAct * kThreads; base < nk; base += kMaxAct * kThreads) {
+        load_acts(base);
+        load_x(base);
+        fold(base);
+    }
+    __syncthreads();
+
+    // ---- stream this thread's rows through its ring ------------------------
+    uint64_t acc[NS][2];
+#pragma unroll
+    for (int st = 0; st < NS; ++st) acc[st][0] = acc[st][1] = 0ull;
+    for (int i = 0; i < my_rows; ++i) {
+        cp_async_wait<D - 1>();
+        const int rl = grp + i * G;
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+            const uint4 chunk = ring[(st * D + (i % D)) * kThreads + tid];
+            chunk_fma<BITS>(chunk, xs + (rl * NS + st) * KPC, acc[st][0], acc[st][1]);
         }
-        while (walk.next(t, r, nr)) {
-            const int slot = g % kStages;
-            if (!mbar_wait(empty_bar(slot), static_cast<uint32_t>((g / kStages - 1) & 1))) {
-                atomicOr(p.status, kStatusProducerTimeout);
-                return;
-            }
-            mbar_arrive_expect_tx(full_bar(slot), stage_bytes(t, nr));
-            copy_weights(slot, t, r, nr);
-            copy_acts(slot, t, r, nr);
-            ++g;
+        if (i + D < my_rows && col_ok)
+#pragma unroll
+            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i + D), src(st, i + D));
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+
+    // ---- reduce: row groups in shared memory, scalars across the CTA -------
+#pragma unroll
+    for (int st = 0; st < NS; ++st) {
+        const float2 a = f2_unpack(acc[st][0]), b = f2_unpack(acc[st][1]);
+        red[st][tid] = (a.x + a.y) + (b.x + b.y);
+    }
+    {
+        const float w0 = warp_sum(ss), w1 = warp_sum(cz[0]), w2 = NS == 2 ? warp_sum(cz[NS - 1]) : 0.f;
+        if (lane == 0) {
+            wred[warp][0] = w0;
+            wred[warp][1] = w1;
+            wred[warp][2] = w2;
+        }
+    }
+    __syncthreads();
+
+    // ---- cluster reduction: every rank deposits its partials in rank 0's
+    // shared memory and leaves; rank 0 waits for S-1 deposits and finalises.
+    if (S > 1) cluster_wait_acquire();
+    const int pstride = NS * C + 4;  // floats per rank slot
+    const uint32_t slot0 = smem_addr(rbuf) + static_cast<uint32_t>(rank * pstride * 4);
+    const uint32_t dst = S > 1 ? map_cluster_addr(slot0, 0) : slot0;
+    if (tid < C) {
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+            float v = 0.f;
+            for (int g = 0; g < G; ++g) v += red[st][g * C + tid];
+            if (rank == 0) rbuf[st * C + tid] = v;
+            else st_cluster_f32(dst + 4u * (st * C + tid), v);
+        }
+    }
+    if (tid < 3) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) v += wred[w][tid];
+        if (rank == 0) rbuf[NS * C + tid] = v;
+        else st_cluster_f32(dst + 4u * (NS * C + tid), v);
+    }
+    if (rank != 0) {
+        __syncthreads();
+        if (tid == 0) {
+            fence_acq_rel_cluster();
+            mbar_arrive_remote(map_cluster_addr(smem_addr(&red_bar), 0));
         }
         return;
     }
-
-    // ------------------------------ consumers -------------------------------
-    pdl_wait();
-    const int col = tid;  // 0..255
-    StageWalk walk{u0, u1, p.R, SR};
-    int t, r, nr;
-    bool have = walk.next(t, r, nr);
-    int frag_r0 = r;
-    uint64_t acc[NS][2];
-    float ss = 0.f, cz[NS];
-#pragma unroll
-    for (int st = 0; st < NS; ++st) {
-        acc[st][0] = acc[st][1] = 0ull;
-        cz[st] = 0.f;
+    if (S > 1) {
+        if (tid == 0) {
+            bool ok = false;
+            for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
+            if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
+        }
     }
-    bool ok = true;
-    for (int g = 0; have; ++g) {
-        const int slot = g % kStages;
-        uint8_t* sp = slots + slot * G::kSlotBytes;
-        if (!mbar_wait(full_bar(slot), static_cast<uint32_t>((g / kStages) & 1))) {
-            if (ok && lane == 0) atomicOr(p.status, kStatusConsumerTimeout);
-            ok = false;
-        }
-        // Fold scales into the activations of this stage.
-        const float* ax = reinterpret_cast<const float*>(sp + G::kOffX);
-        const float* ag = reinterpret_cast<const float*>(sp + G::kOffGamma);
-        float* xp = reinterpret_cast<float*>(sp + G::kOffXp);
-        const int n = nr * KPC;
-        for (int i = tid; i < n; i += kConsumers) {
-            const float xv = ax[i];
-            float xg = xv;
-            if constexpr (kNorm) {
-                ss = fmaf(xv, xv, ss);
-                xg = xv * ag[i];
-            }
+    __syncthreads();
+    if (tid < C || warp == 0) {
+        const bool active = tid < C;
+        float a[NS], tot[3] = {0.f, 0.f, 0.f};
 #pragma unroll
-            for (int st = 0; st < NS; ++st) {
-                float v = xg;
-                if constexpr (kQuant) {
-                    const float* as = reinterpret_cast<const float*>(sp + G::kOffS) + st * SA;
-                    const float* az = reinterpret_cast<const float*>(sp + G::kOffZ) + st * SA;
-                    v = xg * as[i];
-                    cz[st] = fmaf(xg, az[i], cz[st]);
-                }
-                if constexpr (BITS == 4) v *= int4_prescale(i);
-                xp[st * SA + i] = v;
+        for (int st = 0; st < NS; ++st) a[st] = 0.f;
+        if (active) {
+            for (int q = 0; q < S; ++q) {
+                const float* rp = rbuf + q * pstride;
+#pragma unroll
+                for (int st = 0; st < NS; ++st) a[st] += rp[st * C + tid];
+                tot[0] += rp[NS * C];
+                tot[1] += rp[NS * C + 1];
+                tot[2] += rp[NS * C + 2];
             }
         }
-        named_sync(kConsumerBar, kConsumers);
-        const uint4* wsm = reinterpret_cast<const uint4*>(sp);
-        for (int i = 0; i < nr; ++i) {
-#pragma unroll
-            for (int st = 0; st < NS; ++st)
-                chunk_fma<BITS>(wsm[(st * SR + i) * kCols + col], xp + st * SA + i * KPC, acc[st][0],
-                                acc[st][1]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(slot));
-
-        int t2 = -1, r2 = 0, nr2 = 0;
-        const bool have2 = walk.next(t2, r2, nr2);
-        if (!have2 || t2 != t) {
-            // -------- end of this CTA's fragment of tile t: rows [frag_r0, r+nr)
-            float a[NS];
-#pragma unroll
-            for (int st = 0; st < NS; ++st) {
-                const float2 x0 = f2_unpack(acc[st][0]), x1 = f2_unpack(acc[st][1]);
-                a[st] = (x0.x + x0.y) + (x1.x + x1.y);
-                acc[st][0] = acc[st][1] = 0ull;
-            }
-            float sc[3] = {warp_sum(ss), warp_sum(cz[0]), NS == 2 ? warp_sum(cz[NS - 1]) : 0.f};
-            if (lane == 0) {
-                red[warp][0] = sc[0];
-                red[warp][1] = sc[1];
-                red[warp][2] = sc[2];
-            }
-            named_sync(kConsumerBar, kConsumers);
-            float tot[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) {
-                tot[0] += red[w][0];
-                tot[1] += red[w][1];
-                tot[2] += red[w][2];
-            }
-            ss = 0.f;
-#pragma unroll
-            for (int st = 0; st < NS; ++st) cz[st] = 0.f;
-            if (frag_r0 == 0 && r + nr == p.R) {
-                finalize<MODE, NS, kQuant, kNorm>(p, t, col, a, tot);
-            } else {
-                const long long tu = static_cast<long long>(t) * p.R;
-                const int first = cta_of(tu, T, P);
-                const int nslots = cta_of(tu + p.R - 1, T, P) - first + 1;
-                const size_t stride = NS * kCols + 4;
-                float* part = p.partial + (static_cast<size_t>(t) * p.max_slots + (cta - first)) * stride;
-#pragma unroll
-                for (int st = 0; st < NS; ++st) part[st * kCols + col] = a[st];
-                if (tid < 3) part[NS * kCols + tid] = tot[tid];
-                __threadfence();
-                named_sync(kConsumerBar, kConsumers);
-                if (tid == 0) s_last = atomicAdd(p.tickets + t, 1u) == static_cast<uint32_t>(nslots - 1);
-                named_sync(kConsumerBar, kConsumers);
-                if (s_last) {
-                    __threadfence();
-                    float sa[NS], st3[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int st = 0; st < NS; ++st) sa[st] = 0.f;
-                    const float* base = p.partial + static_cast<size_t>(t) * p.max_slots * stride;
-                    for (int q = 0; q < nslots; ++q) {
-                        const float* pq = base + q * stride;
-#pragma unroll
-                        for (int st = 0; st < NS; ++st) sa[st] += __ldcg(pq + st * kCols + col);
-                        st3[0] += __ldcg(pq + NS * kCols);
-                        st3[1] += __ldcg(pq + NS * kCols + 1);
-                        st3[2] += __ldcg(pq + NS * kCols + 2);
-                    }
-                    finalize<MODE, NS, kQuant, kNorm>(p, t, col, sa, st3);
-                    if (tid == 0) atomicExch(p.tickets + t, 0u);
-                }
-            }
-            frag_r0 = r2;
-        }
-        t = t2;
-        r = r2;
-        nr = nr2;
-        have = have2;
+        finalize<MODE, NS, kQuant, kNorm>(p, col0 + tid, active, a, tot);
     }
 }
 
@@ -464,43 +426,45 @@ int sm_count(int* out) {
 template <int BITS, int MODE>
 int launch_one(const GemvParams& p0, cudaStream_t stream) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
-    using G = Geometry<BITS, NS>;
+    constexpr int KPC = 128 / BITS;
     GemvParams p = p0;
-    p.R = p.K / G::KPC;
-    p.tiles = (p.N + kCols - 1) / kCols;
-    const long long T = static_cast<long long>(p.tiles) * p.R;
+    p.R = p.K / KPC;
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
-    const int P = static_cast<int>(T < static_cast<long long>(kCtasPerSm) * sms ? T : kCtasPerSm * sms);
-    int max_slots = 1;
-    for (int t = 0; t < p.tiles; ++t) {
-        const long long tu = static_cast<long long>(t) * p.R;
-        const int n = cta_of(tu + p.R - 1, T, P) - cta_of(tu, T, P) + 1;
-        max_slots = n > max_slots ? n : max_slots;
+    // Widest tile and smallest cluster that put at least two CTAs on every SM.
+    int C = 32, S = 8;
+    bool found = false;
+    for (int cw = 256; cw >= 32 && !found; cw /= 2)
+        for (int s = 1; s <= 8 && !found; s *= 2) {
+            const long long ctas = static_cast<long long>((p.N + cw - 1) / cw) * s;
+            if (ctas >= 2LL * sms) {
+                C = cw;
+                S = s;
+                found = true;
+            }
+        }
+    p.rows_cta = (p.R + S - 1) / S;
+    while (S > 1 && (S - 1) * p.rows_cta >= p.R) {  // no empty ranks
+        S /= 2;
+        p.rows_cta = (p.R + S - 1) / S;
     }
-    p.max_slots = max_slots;
-    const size_t ticket_bytes = (static_cast<size_t>(p.tiles) * 4 + 255) / 256 * 256;
-    const size_t part_bytes = static_cast<size_t>(p.tiles) * max_slots * (NS * kCols + 4) * sizeof(float);
-    void* ws = nullptr;
-    if (int e = device_workspace(kWorkspaceHeader + ticket_bytes + part_bytes, &ws, stream)) return e;
-    p.status = static_cast<uint32_t*>(ws);
-    p.tickets = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + kWorkspaceHeader);
-    p.partial = reinterpret_cast<float*>(static_cast<char*>(ws) + kWorkspaceHeader + ticket_bytes);
-
+    p.cols = C;
+    p.rbuf_floats = (S * (NS * C + 4) + 3) / 4 * 4;
+    const size_t smem = kRingBytes + (static_cast<size_t>(p.rbuf_floats) + static_cast<size_t>(p.rows_cta) * NS * KPC) * sizeof(float);
+    if (smem > 200 * 1024)
+        return set_error(kErrUnsupported, "K=%d is too long for one launch (%zu bytes of staged activations)", p.K,
+                         smem);
     auto kern = gemv_kernel<BITS, MODE>;
-    static bool attr_set = false;  // one instantiation per (BITS, MODE)
-    if (!attr_set) {
-        VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes));
-        attr_set = true;
-    }
+    if (smem > 48 * 1024)
+        VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(P, 1, 1);
+    cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = G::kSmemBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
-    cfg.numAttrs = launch_attrs(attrs, 1);
+    cfg.numAttrs = launch_attrs(attrs, S);
     VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
     return kOk;
 }
@@ -528,7 +492,7 @@ int check_common(int bits, int N, int K, const void* w, const float* s, const fl
     if (misaligned(w) || misaligned(x) || (gamma && misaligned(gamma)))
         return set_error(kErrArg, "weights, x and gamma must be 16-byte aligned");
     if (bits <= 8) {
-        if (N % kCols != 0) return set_error(kErrArg, "N=%d must be a multiple of 256 for quantised weights", N);
+        if (N % kGroup != 0) return set_error(kErrArg, "N=%d must be a multiple of 256 for quantised weights", N);
         if (!s || !z) return set_error(kErrArg, "quantised weights need scale and zero arrays");
         if (misaligned(s) || misaligned(z)) return set_error(kErrArg, "scale and zero must be 16-byte aligned");
     }
@@ -630,16 +594,16 @@ int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* z
     return launch_mode<kSwiglu>(bits, p, static_cast<cudaStream_t>(stream));
 }
 
-// Status word of the library workspace on the current device: bit 0 a
-// producer wait, bit 1 a consumer wait gave up.  Reading waits for the
+// Status word of the current device (bits: kStatus*).  Reading waits for the
 // device; `clear` resets it.
 int vkc_device_status(unsigned* status, int clear) {
-    void* ws = nullptr;
-    if (int e = device_workspace(kWorkspaceHeader, &ws, nullptr)) return e;
     VKC_CUDA_TRY(cudaDeviceSynchronize());
     uint32_t v = 0;
-    VKC_CUDA_TRY(cudaMemcpy(&v, ws, sizeof v, cudaMemcpyDeviceToHost));
-    if (clear) VKC_CUDA_TRY(cudaMemset(ws, 0, sizeof v));
+    VKC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_status, sizeof v));
+    if (clear) {
+        const uint32_t zero = 0;
+        VKC_CUDA_TRY(cudaMemcpyToSymbol(g_status, &zero, sizeof zero));
+    }
     *status = v;
     return kOk;
 }
