@@ -49,7 +49,10 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kGroup = 256;     // outputs per scale block
 constexpr int kCtasPerSm = 4;   // occupancy target (64 registers per thread)
-constexpr int kRingBytes = 32768;  // cp.async ring per CTA (all streams)
+// cp.async ring per CTA (all streams): deeper for the quantised widths,
+// whose CTAs are fewer per SM.
+template <int BITS>
+constexpr int ring_bytes() { return BITS <= 8 ? 49152 : 32768; }
 
 enum Mode : int {
     kGemv = 0,       // shader/GEMV-*.comp
@@ -99,16 +102,40 @@ __device__ __forceinline__ float int4_prescale(int t) {
 constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
 __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(kMagic | bits); }
 
+// Two exact codes as an f32x2 pair (2^23 + code, both halves built in one asm
+// block so the pair lands in a register pair without moves).  int4: each half
+// is (word & mask) | 2^23; int8: each half is byte `sel` of the word under 2^23.
+__device__ __forceinline__ uint64_t nib_pair(uint32_t a, uint32_t ma, uint32_t b, uint32_t mb) {
+    uint64_t r;
+    asm("{\n\t.reg .b32 lo, hi;\n\t"
+        "lop3.b32 lo, %1, %2, %5, 0xEA;\n\t"
+        "lop3.b32 hi, %3, %4, %5, 0xEA;\n\t"
+        "mov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r)
+        : "r"(a), "r"(ma), "r"(b), "r"(mb), "r"(kMagic));
+    return r;
+}
+template <uint32_t SEL_LO, uint32_t SEL_HI>
+__device__ __forceinline__ uint64_t byte_pair(uint32_t w) {
+    uint64_t r;
+    asm("{\n\t.reg .b32 lo, hi;\n\t"
+        "prmt.b32 lo, %1, %2, %3;\n\t"
+        "prmt.b32 hi, %1, %2, %4;\n\t"
+        "mov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r)
+        : "r"(w), "r"(kMagic), "n"(SEL_LO), "n"(SEL_HI));
+    return r;
+}
+
 // One chunk of KPC weights of one column against the staged activations xs
-// (16-byte aligned shared memory); accumulates into the pair accumulators.
+// (16-byte aligned shared memory); accumulates into four pair accumulators.
 template <int BITS>
-__device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict__ xs, uint64_t& a0,
-                                          uint64_t& a1) {
+__device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict__ xs, uint64_t (&a)[4]) {
     const float4* x4 = reinterpret_cast<const float4*>(xs);
     if constexpr (BITS == 32) {
         const float4 v = x4[0];
-        a0 = f2_fma(f2_pack(v.x, v.y), f2_pack(__uint_as_float(c.x), __uint_as_float(c.y)), a0);
-        a1 = f2_fma(f2_pack(v.z, v.w), f2_pack(__uint_as_float(c.z), __uint_as_float(c.w)), a1);
+        a[0] = f2_fma(f2_pack(v.x, v.y), f2_pack(__uint_as_float(c.x), __uint_as_float(c.y)), a[0]);
+        a[1] = f2_fma(f2_pack(v.z, v.w), f2_pack(__uint_as_float(c.z), __uint_as_float(c.w)), a[1]);
     } else if constexpr (BITS == 16) {
         const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
@@ -116,8 +143,8 @@ __device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict
             const float4 v = x4[q];
             const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&wd[2 * q]));
             const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&wd[2 * q + 1]));
-            a0 = f2_fma(f2_pack(v.x, v.y), f2_pack(w0.x, w0.y), a0);
-            a1 = f2_fma(f2_pack(v.z, v.w), f2_pack(w1.x, w1.y), a1);
+            a[2 * q] = f2_fma(f2_pack(v.x, v.y), f2_pack(w0.x, w0.y), a[2 * q]);
+            a[2 * q + 1] = f2_fma(f2_pack(v.z, v.w), f2_pack(w1.x, w1.y), a[2 * q + 1]);
         }
     } else if constexpr (BITS == 8) {
         const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
@@ -126,14 +153,8 @@ __device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict
         for (int q = 0; q < 4; ++q) {
             const float4 v = x4[q];
             const uint32_t w = wd[q];
-            const uint64_t p01 = f2_add(f2_pack(__uint_as_float(__byte_perm(w, kMagic, 0x7540)),
-                                                __uint_as_float(__byte_perm(w, kMagic, 0x7541))),
-                                        neg);
-            const uint64_t p23 = f2_add(f2_pack(__uint_as_float(__byte_perm(w, kMagic, 0x7542)),
-                                                __uint_as_float(__byte_perm(w, kMagic, 0x7543))),
-                                        neg);
-            a0 = f2_fma(f2_pack(v.x, v.y), p01, a0);
-            a1 = f2_fma(f2_pack(v.z, v.w), p23, a1);
+            a[q] = f2_fma(f2_pack(v.x, v.y), f2_add(byte_pair<0x7540, 0x7541>(w), neg), a[q]);
+            a[q] = f2_fma(f2_pack(v.z, v.w), f2_add(byte_pair<0x7542, 0x7543>(w), neg), a[q]);
         }
     } else {  // BITS == 4
         const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
@@ -144,14 +165,10 @@ __device__ __forceinline__ void chunk_fma(const uint4 c, const float* __restrict
             const float4 v1 = x4[2 * q + 1];
             const uint32_t w = wd[q];
             const uint32_t h = w >> 12;
-            const uint64_t p01 = f2_add(f2_pack(magic_f(w & 0xFu), magic_f(w & 0xF0u)), neg);
-            const uint64_t p23 = f2_add(f2_pack(magic_f(w & 0xF00u), magic_f(w & 0xF000u)), neg);
-            const uint64_t p45 = f2_add(f2_pack(magic_f(w & 0xF0000u), magic_f(h & 0xF00u)), neg);
-            const uint64_t p67 = f2_add(f2_pack(magic_f(h & 0xF000u), magic_f(h & 0xF0000u)), neg);
-            a0 = f2_fma(f2_pack(v0.x, v0.y), p01, a0);
-            a1 = f2_fma(f2_pack(v0.z, v0.w), p23, a1);
-            a0 = f2_fma(f2_pack(v1.x, v1.y), p45, a0);
-            a1 = f2_fma(f2_pack(v1.z, v1.w), p67, a1);
+            a[0] = f2_fma(f2_pack(v0.x, v0.y), f2_add(nib_pair(w, 0xFu, w, 0xF0u), neg), a[0]);
+            a[1] = f2_fma(f2_pack(v0.z, v0.w), f2_add(nib_pair(w, 0xF00u, w, 0xF000u), neg), a[1]);
+            a[2] = f2_fma(f2_pack(v1.x, v1.y), f2_add(nib_pair(w, 0xF0000u, h, 0xF00u), neg), a[2]);
+            a[3] = f2_fma(f2_pack(v1.z, v1.w), f2_add(nib_pair(h, 0xF000u, h, 0xF0000u), neg), a[3]);
         }
     }
 }
@@ -193,13 +210,13 @@ template <int BITS, int MODE>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvParams p) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
     constexpr int KPC = 128 / BITS;
-    constexpr int D = kRingBytes / (NS * kThreads * 16);  // rows in flight per thread
+    constexpr int D = ring_bytes<BITS>() / (NS * kThreads * 16);  // rows in flight per thread
     constexpr bool kQuant = BITS <= 8;
     constexpr bool kNorm = MODE != kGemv;
 
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* ring = reinterpret_cast<uint4*>(smem);                         // [NS][D][256]
-    float* rbuf = reinterpret_cast<float*>(smem + kRingBytes);             // [S][NS*C + 4] (rank 0)
+    float* rbuf = reinterpret_cast<float*>(smem + ring_bytes<BITS>());     // [S][NS*C + 4] (rank 0)
     float* xs = rbuf + p.rbuf_floats;                                      // [rows_cta][NS][KPC]
     __shared__ float red[NS][kThreads];                                    // row-group partials
     __shared__ float wred[kThreads / 32][3];
@@ -315,16 +332,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
     __syncthreads();
 
     // ---- stream this thread's rows through its ring ------------------------
-    uint64_t acc[NS][2];
+    uint64_t acc[NS][4];
 #pragma unroll
-    for (int st = 0; st < NS; ++st) acc[st][0] = acc[st][1] = 0ull;
+    for (int st = 0; st < NS; ++st) acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0ull;
     for (int i = 0; i < my_rows; ++i) {
         cp_async_wait<D - 1>();
         const int rl = grp + i * G;
 #pragma unroll
         for (int st = 0; st < NS; ++st) {
             const uint4 chunk = ring[(st * D + (i % D)) * kThreads + tid];
-            chunk_fma<BITS>(chunk, xs + (rl * NS + st) * KPC, acc[st][0], acc[st][1]);
+            chunk_fma<BITS>(chunk, xs + (rl * NS + st) * KPC, acc[st]);
         }
         if (i + D < my_rows && col_ok)
 #pragma unroll
@@ -337,7 +354,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
 #pragma unroll
     for (int st = 0; st < NS; ++st) {
         const float2 a = f2_unpack(acc[st][0]), b = f2_unpack(acc[st][1]);
-        red[st][tid] = (a.x + a.y) + (b.x + b.y);
+        const float2 c2 = f2_unpack(acc[st][2]), d = f2_unpack(acc[st][3]);
+        red[st][tid] = ((a.x + a.y) + (b.x + b.y)) + ((c2.x + c2.y) + (d.x + d.y));
     }
     {
         const float w0 = warp_sum(ss), w1 = warp_sum(cz[0]), w2 = NS == 2 ? warp_sum(cz[NS - 1]) : 0.f;
@@ -450,7 +468,7 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     }
     p.cols = C;
     p.rbuf_floats = (S * (NS * C + 4) + 3) / 4 * 4;
-    const size_t smem = kRingBytes + (static_cast<size_t>(p.rbuf_floats) + static_cast<size_t>(p.rows_cta) * NS * KPC) * sizeof(float);
+    const size_t smem = ring_bytes<BITS>() + (static_cast<size_t>(p.rbuf_floats) + static_cast<size_t>(p.rows_cta) * NS * KPC) * sizeof(float);
     if (smem > 200 * 1024)
         return set_error(kErrUnsupported, "K=%d is too long for one launch (%zu bytes of staged activations)", p.K,
                          smem);
