@@ -99,6 +99,23 @@ int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const vo
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference.
+ * For callers that cannot allocate device memory when attention runs (an
+ * engine whose memory pool already owns all of HBM, a decode loop that must not
+ * take the synchronisation cudaMalloc/cudaFree can imply, a plugin whose host
+ * forbids allocation in its callbacks).  Same arguments and results as
+ * vkc_attention_decode, but its scratch is a fixed 2 MiB array inside the
+ * library (held by every GPU that loads the library until it is unloaded);
+ * shapes needing more (vkc_attention_workspace_bytes) are rejected with
+ * VKC_ERR_ARG.  The first call on a device looks up the array's address and
+ * clears its tickets, so make that first call before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU (different streams)
+ * race; calls ordered on one stream do not. */
+size_t vkc_attention_noalloc_max_scratch(void);
+int vkc_attention_decode_noalloc(const void* q, int q_bits, const void* kcache, const void* vcache,
+                                 float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
+                                 void* stream);
+
 /* C = A B, row-major fp32 (A M x K, B K x N).  Replaces shader/gemm.comp. */
 int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, void* stream);
 

@@ -25,6 +25,8 @@
 
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 
 namespace vkc {
 namespace {
@@ -343,6 +345,71 @@ int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const vo
     }
     return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, scale,
                             workspace, workspace_bytes, s);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// vkc_attention_decode needs scratch for its split partials and merge tickets:
+// either a buffer the caller allocated or one the library cudaMallocs on first
+// use.  Some callers can do neither at the moment they run attention: an
+// engine that has handed all of HBM to its own pool (weights and KV cache) so
+// a cudaMalloc would fail or fragment it, a decode loop that must not take the
+// device-wide synchronisation cudaMalloc/cudaFree can imply, or a plugin whose
+// host forbids allocations inside its callbacks.  This entry point uses a
+// fixed scratch array that is part of the loaded library image instead.
+// ---------------------------------------------------------------------------
+namespace vkc {
+namespace {
+// Scratch of the allocation-free entry point: 2 MiB, in every device's image
+// of this library for as long as the library stays loaded.  Bytes [0, 256)
+// hold the per-KV-head merge tickets, which must be zero when a call starts;
+// each call leaves them at zero.
+constexpr size_t kNoAllocScratchBytes = 2u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch per device
+
+// Once per device, with that device current: look up the array's device
+// address (in host code its name is only a stand-in) and clear the tickets.
+int noalloc_scratch(void** out, cudaStream_t stream) {
+    int dev = 0;
+    VKC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return set_error(kErrCuda, "cudaGetSymbolAddress(attention scratch) failed: %s", cudaGetErrorString(e));
+        VKC_CUDA_TRY(cudaMemsetAsync(p, 0, kWorkspaceHeader, stream));
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return kOk;
+}
+}  // namespace
+}  // namespace vkc
+
+size_t vkc_attention_noalloc_max_scratch(void) { return kNoAllocScratchBytes; }
+
+int vkc_attention_decode_noalloc(const void* q, int q_bits, const void* kcache, const void* vcache, float* out,
+                                 int n_q, int n_kv, int head_dim, int ctx, float scale, void* stream) {
+    if (n_q <= 0 || n_kv <= 0 || head_dim <= 0 || ctx <= 0)
+        return set_error(kErrArg, "n_q=%d, n_kv=%d, head_dim=%d and ctx=%d must be positive", n_q, n_kv, head_dim,
+                         ctx);
+    const size_t need = attention_workspace_bytes(n_q, n_kv, head_dim, ctx);
+    if (need > kNoAllocScratchBytes)
+        return set_error(kErrArg,
+                         "attention with %d query heads, head_dim %d and context %d needs %zu bytes of scratch; "
+                         "the allocation-free entry point holds %zu (use vkc_attention_decode)",
+                         n_q, head_dim, ctx, need, kNoAllocScratchBytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* scratch = nullptr;
+    if (int e = noalloc_scratch(&scratch, s)) return e;
+    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, scale, scratch,
+                            kNoAllocScratchBytes, s);
 }
 
 }  // extern "C"
