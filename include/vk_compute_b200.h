@@ -65,6 +65,24 @@ int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* z
                      const float* x, const float* gamma, float* y, int N, int K, float eps,
                      int rms_dim, void* stream);
 
+/* y = W^T x + residual (the decoder's O and down projections with their
+ * residual connection fused).  No counterpart in the reference, whose driver
+ * runs one operator and has no residual add. */
+int vkc_gemv_residual(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                      const float* residual, float* y, int N, int K, void* stream);
+
+/* RmsNorm-GEMV-Rope for a decoder's fused QKV projection with the KV-cache
+ * append the reference lacks: outputs are [Q heads | K heads | V heads]
+ * (q_rows, kv_rows, kv_rows rows, whole heads of head_dim); Q and K rotate on
+ * adjacent pairs by pos*theta[p], V does not; all rows are written to y (fp32)
+ * and K/V rows also, as fp16, at token `pos` into kcache K[t][h][d] and
+ * vcache V[h][d/8][t][d%8] (the Att-full-FP16 layouts) of ctx_cap tokens. */
+int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero,
+                             const float* x, const float* gamma, const float* theta, float* y,
+                             int N, int K, float eps, int rms_dim, int pos, int head_dim,
+                             int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
+                             void* stream);
+
 /* RmsNorm-GEMV followed by a rotary epilogue at position `pos`.
  * rope_mode 0: the epilogue of shader/RmsNorm-GEMV-Rope-FP16.comp:76-89 as
  *   written (first 64 outputs of every 256, partner term taken from theta;
@@ -98,6 +116,13 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* vkc_attention_decode over a cache allocated for ctx_cap >= ctx tokens (the
+ * V layout's per-(head, chunk) token run is ctx_cap long); tokens [0, ctx)
+ * are attended.  The decoder chain uses it while its cache fills. */
+int vkc_attention_decode_cache(const void* q, int q_bits, const void* kcache, const void* vcache,
+                               float* out, int n_q, int n_kv, int head_dim, int ctx, int ctx_cap,
+                               float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  * For callers that cannot allocate device memory when attention runs (an

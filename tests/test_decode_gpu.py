@@ -1,0 +1,71 @@
+"""A small decoder chain on the GPU against a reference composed from the
+oracle's operators: two layers, two consecutive tokens (the second attends
+to the KV entries the first appended), int4 weights."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close
+from oracle import pyoracle as o
+from vk_compute_b200.decode import DecoderConfig, ShardedDecoder, dense_weight, rope_theta
+
+pytestmark = pytest.mark.gpu
+
+CFG = DecoderConfig(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64, bits=4)
+
+
+def f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float64)
+
+
+def ref_attention(q, kc, vc, n_q, n_kv, hd, ctx, scale):
+    """q [n_q*hd]; kc [cap][n_kv][hd]; vc [n_kv][hd/8][cap][8] (float)."""
+    out = np.zeros(n_q * hd)
+    g = n_q // n_kv
+    for h in range(n_q):
+        kv = h // g
+        K = kc[:ctx, kv, :]
+        V = vc[kv].transpose(1, 0, 2).reshape(-1, hd)[:ctx]
+        s = K @ q[h * hd:(h + 1) * hd] * scale
+        w = np.exp(s - s.max())
+        out[h * hd:(h + 1) * hd] = (w[:, None] * V).sum(0) / w.sum()
+    return out
+
+
+def test_decoder_two_layers_two_tokens():
+    cfg = CFG
+    dec = ShardedDecoder(cfg, seed=3)
+    H, I, hd = cfg.hidden, cfg.inter, cfg.head_dim
+    # host copies of every layer (same dense matrices, oracle quantiser)
+    host = []
+    for i, L in enumerate(dec.layers):
+        base = 3 * 1000 + i * 10
+        mats = [dense_weight(base + j, *shape, cfg.w_std, "cuda").cpu().numpy()
+                for j, shape in ((1, (H, cfg.qkv_rows)), (2, (H, H)), (3, (H, I)), (4, (H, I)), (5, (I, H)))]
+        q = [o.quantize(m, 4, True, True) for m in mats]
+        host.append(dict(q=q, g_attn=L.g_attn.cpu().numpy(), g_ffn=L.g_ffn.cpu().numpy(),
+                         kc=L.kcache.cpu().numpy().astype(np.float64), vc=L.vcache.cpu().numpy().astype(np.float64)))
+    theta = rope_theta(cfg, "cpu").numpy()
+    x0 = torch.randn(H, generator=torch.Generator().manual_seed(5))
+    dec.buf.x.copy_(x0)
+    x = x0.numpy().astype(np.float64)
+    q_rows, kv_rows = cfg.n_q * hd, cfg.n_kv * hd
+    for pos in (40, 41):
+        out = dec.step(pos).cpu().numpy()
+        for i in range(cfg.layers):
+            hl = host[i]
+            qkv = o.qgemv(x, hl["g_attn"], *hl["q"][0], 4, H, cfg.qkv_rows, H, cfg.eps)
+            qkv = o.rope_pairs(qkv, hd, q_rows + kv_rows, pos, theta).astype(np.float64)
+            hl["kc"][pos] = f16(qkv[q_rows:q_rows + kv_rows]).reshape(cfg.n_kv, hd)
+            v = f16(qkv[q_rows + kv_rows:]).reshape(cfg.n_kv, hd // 8, 8)
+            hl["vc"][:, :, pos, :] = v
+            a = ref_attention(qkv[:q_rows], hl["kc"], hl["vc"], cfg.n_q, cfg.n_kv, hd, pos + 1, 1 / math.sqrt(hd))
+            xm = x + o.qgemv(a, None, *hl["q"][1], 4, H, H)
+            h = o.qswiglu(xm, hl["g_ffn"], hl["q"][2], hl["q"][3], 4, H, I, H, cfg.eps)
+            x = xm + o.qgemv(h, None, *hl["q"][4], 4, I, H)
+        assert_close(out, x, 5e-3, f"decoder output at pos {pos}")
+        # the appended cache entries match
+        kc = dec.layers[-1].kcache.cpu().numpy().astype(np.float64)
+        assert_close(kc[pos], host[-1]["kc"][pos], 5e-3, "K cache append")

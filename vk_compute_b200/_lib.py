@@ -26,8 +26,11 @@ SIGNATURES = {
     "vkc_rmsnorm_gemv": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
     "vkc_rmsnorm_gemv_rope": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p]),
     "vkc_rmsnorm_swiglu": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
+    "vkc_gemv_residual": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _p]),
+    "vkc_rmsnorm_gemv_rope_kv": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p, _p, _i, _p]),
     "vkc_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "vkc_attention_decode": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
+    "vkc_attention_decode_cache": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_gemm_f32": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "vkc_generate": (_i, [_i, _i, _i, _i, _p, _p]),
     "vkc_quantize": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p]),

@@ -43,6 +43,7 @@ struct AttnParams {
     float* ws;          // [n_q][splits][hd + 2] : acc[hd], m, l
     unsigned* tickets;  // [n_kv]
     int n_q, n_kv, hd, ctx, splits, tpc;
+    int ctx_cap;        // V run length per (head, chunk): the cache capacity
     float scale_log2;   // scale * log2(e)
 };
 
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_decode_kernel(const Att
     __syncthreads();
 
     // ---- phase 3: probabilities x V ------------------------------------------
-    const size_t vrun = static_cast<size_t>(p.ctx);  // uint4 per (kv, chunk) run
+    const size_t vrun = static_cast<size_t>(p.ctx_cap);  // uint4 per (kv, chunk) run
     for (int c = warp; c < chunks; c += kAttThreads / 32) {
         float acc[32];
 #pragma unroll
@@ -268,7 +269,7 @@ size_t attention_workspace_bytes(int n_q, int n_kv, int hd, int ctx) {
 }
 
 int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, float* out,
-                     int n_q, int n_kv, int hd, int ctx, float scale, void* ws, size_t ws_bytes,
+                     int n_q, int n_kv, int hd, int ctx, int ctx_cap, float scale, void* ws, size_t ws_bytes,
                      cudaStream_t stream) {
     if (!q || !kc || !vc || !out) return set_error(kErrArg, "null attention pointer");
     if (q_bits != 16 && q_bits != 32) return set_error(kErrArg, "q_bits=%d (expected 16 or 32)", q_bits);
@@ -280,6 +281,7 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     if (hd <= 0 || hd % 8 != 0 || hd > 256)
         return set_error(kErrArg, "head_dim=%d must be a multiple of 8 in [8, 256]", hd);
     if (ctx <= 0) return set_error(kErrArg, "context length %d must be positive", ctx);
+    if (ctx_cap < ctx) return set_error(kErrArg, "cache capacity %d below the context length %d", ctx_cap, ctx);
     if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) |
          reinterpret_cast<uintptr_t>(q)) % 16 != 0)
         return set_error(kErrArg, "q and the K/V caches must be 16-byte aligned");
@@ -301,6 +303,7 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     p.n_kv = n_kv;
     p.hd = hd;
     p.ctx = ctx;
+    p.ctx_cap = ctx_cap;
     p.splits = splits;
     p.tpc = tpc;
     p.scale_log2 = scale * kLog2e;
@@ -343,8 +346,24 @@ int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const vo
         workspace = static_cast<char*>(base) + kWorkspaceHeader;
         workspace_bytes = need;
     }
-    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, scale,
+    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, ctx, scale,
                             workspace, workspace_bytes, s);
+}
+
+int vkc_attention_decode_cache(const void* q, int q_bits, const void* kcache, const void* vcache, float* out,
+                               int n_q, int n_kv, int head_dim, int ctx, int ctx_cap, float scale, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!workspace) {
+        const size_t need = attention_workspace_bytes(n_q > 0 ? n_q : 1, n_kv > 0 ? n_kv : 1,
+                                                      head_dim > 0 ? head_dim : 8, ctx > 0 ? ctx : 1);
+        void* base = nullptr;
+        if (int e = device_workspace(need + kWorkspaceHeader, &base, s)) return e;
+        workspace = static_cast<char*>(base) + kWorkspaceHeader;
+        workspace_bytes = need;
+    }
+    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, ctx_cap, scale, workspace,
+                            workspace_bytes, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -408,7 +427,7 @@ int vkc_attention_decode_noalloc(const void* q, int q_bits, const void* kcache, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* scratch = nullptr;
     if (int e = noalloc_scratch(&scratch, s)) return e;
-    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, scale, scratch,
+    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, ctx, scale, scratch,
                             kNoAllocScratchBytes, s);
 }
 

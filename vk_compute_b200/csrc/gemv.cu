@@ -49,10 +49,10 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kGroup = 256;     // outputs per scale block
 constexpr int kCtasPerSm = 4;   // occupancy target (64 registers per thread)
-// cp.async ring per CTA (all streams): deeper for the quantised widths,
-// whose CTAs are fewer per SM.
-template <int BITS>
-constexpr int ring_bytes() { return BITS <= 8 ? 49152 : 32768; }
+// cp.async ring per CTA (all streams): 32 KB, or 48 KB when the grid still
+// fits on the GPU in one wave with the deeper ring.
+template <bool DEEP>
+constexpr int ring_bytes() { return DEEP ? 49152 : 32768; }
 
 enum Mode : int {
     kGemv = 0,       // shader/GEMV-*.comp
@@ -79,6 +79,14 @@ struct GemvParams {
     int pos;
     int head_dim;
     int rot_rows;
+    const float* residual;  // optional: y[j] += residual[j] (plain GEMV)
+    // Optional KV-cache append (rotary-pairs mode): outputs [q_rows, q_rows +
+    // kv_rows) are K heads, the next kv_rows are V heads; both are also stored
+    // as fp16 at token `pos` into K[t][h][d] and V[h][d/8][t][d%8] caches of
+    // `ctx_cap` tokens.
+    uint16_t* kcache;
+    uint16_t* vcache;
+    int q_rows, kv_rows, ctx_cap;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -203,20 +211,39 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
         // shader/RmsNorm-swiglu-ffn-FP16.comp:86-87
         out = out / (1.0f + exp2f(-out * 1.44269504f)) * v[1];
     }
-    if (active && j < p.N) p.y[j] = out;
+    if constexpr (MODE == kGemv) {
+        if (p.residual && active && j < p.N) out += p.residual[j];
+    }
+    if (active && j < p.N) {
+        p.y[j] = out;
+        if constexpr (MODE == kRopePairs) {
+            if (p.kcache && j >= p.q_rows) {
+                const int jj = j - p.q_rows;
+                const int hd = p.head_dim;
+                const uint16_t bits = __half_as_ushort(__float2half_rn(out));
+                if (jj < p.kv_rows) {
+                    const int h = jj / hd, d = jj % hd;
+                    p.kcache[(static_cast<size_t>(p.pos) * (p.kv_rows / hd) + h) * hd + d] = bits;
+                } else if (jj < 2 * p.kv_rows) {
+                    const int h = (jj - p.kv_rows) / hd, d = (jj - p.kv_rows) % hd;
+                    p.vcache[((static_cast<size_t>(h) * (hd / 8) + d / 8) * p.ctx_cap + p.pos) * 8 + d % 8] = bits;
+                }
+            }
+        }
+    }
 }
 
-template <int BITS, int MODE>
+template <int BITS, int MODE, bool DEEP>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvParams p) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
     constexpr int KPC = 128 / BITS;
-    constexpr int D = ring_bytes<BITS>() / (NS * kThreads * 16);  // rows in flight per thread
+    constexpr int D = ring_bytes<DEEP>() / (NS * kThreads * 16);  // rows in flight per thread
     constexpr bool kQuant = BITS <= 8;
     constexpr bool kNorm = MODE != kGemv;
 
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* ring = reinterpret_cast<uint4*>(smem);                         // [NS][D][256]
-    float* rbuf = reinterpret_cast<float*>(smem + ring_bytes<BITS>());     // [S][NS*C + 4] (rank 0)
+    float* rbuf = reinterpret_cast<float*>(smem + ring_bytes<DEEP>());     // [S][NS*C + 4] (rank 0)
     float* xs = rbuf + p.rbuf_floats;                                      // [rows_cta][NS][KPC]
     __shared__ float red[NS][kThreads];                                    // row-group partials
     __shared__ float wred[kThreads / 32][3];
@@ -468,23 +495,31 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     }
     p.cols = C;
     p.rbuf_floats = (S * (NS * C + 4) + 3) / 4 * 4;
-    const size_t smem = ring_bytes<BITS>() + (static_cast<size_t>(p.rbuf_floats) + static_cast<size_t>(p.rows_cta) * NS * KPC) * sizeof(float);
+    const size_t rest = (static_cast<size_t>(p.rbuf_floats) + static_cast<size_t>(p.rows_cta) * NS * KPC) * sizeof(float);
+    const long long ctas = static_cast<long long>(S) * ((p.N + C - 1) / C);
+    const long long per_sm = (ctas + sms - 1) / sms;
+    // Deep ring only if every CTA is still resident at once (static shared
+    // memory and the per-CTA reservation take about 3 KB more).
+    const bool deep = per_sm * (ring_bytes<true>() + rest + 3072) <= 227 * 1024 && per_sm <= kCtasPerSm;
+    const size_t smem = (deep ? ring_bytes<true>() : ring_bytes<false>()) + rest;
     if (smem > 200 * 1024)
         return set_error(kErrUnsupported, "K=%d is too long for one launch (%zu bytes of staged activations)", p.K,
                          smem);
-    auto kern = gemv_kernel<BITS, MODE>;
-    if (smem > 48 * 1024)
-        VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attrs[2];
-    cfg.attrs = attrs;
-    cfg.numAttrs = launch_attrs(attrs, S);
-    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
-    return kOk;
+    auto go = [&](auto kern) -> int {
+        if (smem > 48 * 1024)
+            VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attrs[2];
+        cfg.attrs = attrs;
+        cfg.numAttrs = launch_attrs(attrs, S);
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+        return kOk;
+    };
+    return deep ? go(gemv_kernel<BITS, MODE, true>) : go(gemv_kernel<BITS, MODE, false>);
 }
 
 template <int MODE>
@@ -536,6 +571,58 @@ int vkc_gemv(int bits, const void* w, const float* scale, const float* zero, con
     p.N = N;
     p.K = K;
     return launch_mode<kGemv>(bits, p, static_cast<cudaStream_t>(stream));
+}
+
+int vkc_gemv_residual(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                      const float* residual, float* y, int N, int K, void* stream) {
+    if (!residual) return set_error(kErrArg, "null residual");
+    if (int e = check_common(bits, N, K, w, scale, zero, x, y, nullptr)) return e;
+    GemvParams p = {};
+    p.w[0] = static_cast<const uint8_t*>(w);
+    p.s[0] = scale;
+    p.z[0] = zero;
+    p.x = x;
+    p.y = y;
+    p.residual = residual;
+    p.N = N;
+    p.K = K;
+    return launch_mode<kGemv>(bits, p, static_cast<cudaStream_t>(stream));
+}
+
+int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                             const float* gamma, const float* theta, float* y, int N, int K, float eps,
+                             int rms_dim, int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
+                             void* vcache, int ctx_cap, void* stream) {
+    if (!gamma || !theta || !kcache || !vcache) return set_error(kErrArg, "null gamma, theta or cache");
+    if (int e = check_common(bits, N, K, w, scale, zero, x, y, gamma)) return e;
+    if (rms_dim <= 0) return set_error(kErrArg, "rms_dim=%d must be positive", rms_dim);
+    if (head_dim <= 0 || head_dim % 8 != 0)
+        return set_error(kErrArg, "head_dim=%d must be a positive multiple of 8", head_dim);
+    if (q_rows < 0 || kv_rows <= 0 || q_rows % head_dim || kv_rows % head_dim || q_rows + 2 * kv_rows != N)
+        return set_error(kErrArg, "rows must be q_rows + 2*kv_rows = N in whole heads (q=%d kv=%d N=%d)", q_rows,
+                         kv_rows, N);
+    if (pos < 0 || pos >= ctx_cap) return set_error(kErrArg, "pos=%d outside the cache of %d tokens", pos, ctx_cap);
+    GemvParams p = {};
+    p.w[0] = static_cast<const uint8_t*>(w);
+    p.s[0] = scale;
+    p.z[0] = zero;
+    p.x = x;
+    p.gamma = gamma;
+    p.theta = theta;
+    p.y = y;
+    p.N = N;
+    p.K = K;
+    p.eps = eps;
+    p.inv_dim = 1.0f / static_cast<float>(rms_dim);
+    p.pos = pos;
+    p.head_dim = head_dim;
+    p.rot_rows = q_rows + kv_rows;  // Q and K rotate, V does not
+    p.kcache = static_cast<uint16_t*>(kcache);
+    p.vcache = static_cast<uint16_t*>(vcache);
+    p.q_rows = q_rows;
+    p.kv_rows = kv_rows;
+    p.ctx_cap = ctx_cap;
+    return launch_mode<kRopePairs>(bits, p, static_cast<cudaStream_t>(stream));
 }
 
 int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* zero, const float* x,

@@ -1,0 +1,241 @@
+"""Row-sharded decoder chain built from the decode-path operators.
+
+One decode step of a stack of transformer layers, each
+
+    qkv  = RmsNorm-GEMV-Rope(W_qkv, x, gamma_attn)   Q,K rotated; K,V appended
+                                                     to the fp16 caches at `pos`
+    a    = Att-full(q, K cache, V cache)             (GQA, split-KV)
+    x'   = x + W_o a
+    h    = RmsNorm-SwiGLU(W_gate, W_up, x', gamma_ffn)
+    x''  = x' + W_down h
+
+with int4 (or int8 / fp16) weights in vk-compute's storage.  The reference
+ships these operators as separate shaders and no driver chains them
+(shader/RmsNorm-GEMV-Rope-*.comp, Att-full-FP16.comp, GEMV-*.comp,
+RmsNorm-swiglu-ffn-*.comp); the chain, the KV append and the residual adds are
+this library's.
+
+Sharding over `world` GPUs of one node (one process each): rank r owns query
+heads [r*nq/world, (r+1)*nq/world) and the matching KV heads, so QKV,
+RoPE, the cache and attention are local; the O, gate/up and down projections
+are split by output rows.  Four all-gathers per layer assemble the attention
+output, x', h and x'' from the ranks' slices.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ops
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    hidden: int = 4096
+    inter: int = 12288
+    n_q: int = 32
+    n_kv: int = 8
+    head_dim: int = 128
+    layers: int = 36
+    ctx: int = 8192          # KV-cache capacity (tokens)
+    bits: int = 4
+    eps: float = 1e-6
+    theta_base: float = 1e6
+    w_std: float = 0.02
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.n_q + 2 * self.n_kv) * self.head_dim
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """Which rows of each weight a rank owns."""
+
+    rank: int
+    world: int
+    q_heads: tuple[int, int]     # [lo, hi) query heads
+    kv_heads: tuple[int, int]    # [lo, hi) KV heads
+    qkv_cols: tuple[int, ...]    # output rows of the full QKV matrix, shard order [Q | K | V]
+    o_rows: tuple[int, int]      # [lo, hi) of hidden
+    ffn_rows: tuple[int, int]    # [lo, hi) of inter
+
+    @property
+    def n_q(self) -> int:
+        return self.q_heads[1] - self.q_heads[0]
+
+    @property
+    def n_kv(self) -> int:
+        return self.kv_heads[1] - self.kv_heads[0]
+
+
+def shard_plan(cfg: DecoderConfig, rank: int, world: int) -> ShardPlan:
+    """Head-aligned shard of rank `rank` out of `world`; raises ValueError when
+    the model does not split evenly into whole heads and 256-row scale blocks."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    if cfg.n_q % world or cfg.n_kv % world:
+        raise ValueError(f"{cfg.n_q} query / {cfg.n_kv} KV heads do not split over {world} ranks")
+    if cfg.hidden % world or cfg.inter % world:
+        raise ValueError(f"hidden {cfg.hidden} / inter {cfg.inter} do not split over {world} ranks")
+    hd = cfg.head_dim
+    nq, nkv = cfg.n_q // world, cfg.n_kv // world
+    q0, k0 = rank * nq, rank * nkv
+    q_cols = range(q0 * hd, (q0 + nq) * hd)
+    k_cols = range(cfg.n_q * hd + k0 * hd, cfg.n_q * hd + (k0 + nkv) * hd)
+    v_cols = range((cfg.n_q + cfg.n_kv) * hd + k0 * hd, (cfg.n_q + cfg.n_kv) * hd + (k0 + nkv) * hd)
+    h = cfg.hidden // world
+    f = cfg.inter // world
+    plan = ShardPlan(rank, world, (q0, q0 + nq), (k0, k0 + nkv), tuple(q_cols) + tuple(k_cols) + tuple(v_cols),
+                     (rank * h, (rank + 1) * h), (rank * f, (rank + 1) * f))
+    if cfg.bits <= 8:
+        for n in (len(plan.qkv_cols), h, f):
+            if n % 256:
+                raise ValueError(f"a {cfg.bits}-bit shard of {n} rows is not a whole number of 256-row scale blocks")
+    return plan
+
+
+def rope_theta(cfg: DecoderConfig, device) -> torch.Tensor:
+    p = torch.arange(cfg.head_dim // 2, dtype=torch.float64)
+    return (cfg.theta_base ** (-2.0 * p / cfg.head_dim)).to(torch.float32).to(device)
+
+
+def dense_weight(seed: int, K: int, N: int, std: float, device) -> torch.Tensor:
+    """Seeded N(0, std) K x N matrix (y = W^T x), generated on the device."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(K, N, generator=g, device=device) * std
+
+
+@dataclass
+class LayerShard:
+    qkv: ops.PackedWeight
+    o: ops.PackedWeight
+    gate: ops.PackedWeight
+    up: ops.PackedWeight
+    down: ops.PackedWeight
+    g_attn: torch.Tensor
+    g_ffn: torch.Tensor
+    kcache: torch.Tensor      # fp16 bits [ctx][n_kv][hd]
+    vcache: torch.Tensor      # fp16 bits [n_kv][hd/8][ctx][8]
+
+
+def _pack(w: torch.Tensor, bits: int) -> ops.PackedWeight:
+    return ops.pack_dense(w, bits, symmetric=True, fp16_scale=True)
+
+
+def build_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: int = 0) -> LayerShard:
+    """Random-init weights of one layer, this rank's shard.  Every rank draws
+    the same full matrices from the same seeds and keeps its own rows, so the
+    sharded model equals the unsharded one."""
+    base = seed * 1000 + layer * 10
+    H, I = cfg.hidden, cfg.inter
+    cols = torch.tensor(plan.qkv_cols, device=device)
+    qkv = _pack(dense_weight(base + 1, H, cfg.qkv_rows, cfg.w_std, device)[:, cols].contiguous(), cfg.bits)
+    o_lo, o_hi = plan.o_rows
+    f_lo, f_hi = plan.ffn_rows
+    o = _pack(dense_weight(base + 2, H, H, cfg.w_std, device)[:, o_lo:o_hi].contiguous(), cfg.bits)
+    gate = _pack(dense_weight(base + 3, H, I, cfg.w_std, device)[:, f_lo:f_hi].contiguous(), cfg.bits)
+    up = _pack(dense_weight(base + 4, H, I, cfg.w_std, device)[:, f_lo:f_hi].contiguous(), cfg.bits)
+    down = _pack(dense_weight(base + 5, I, H, cfg.w_std, device)[:, o_lo:o_hi].contiguous(), cfg.bits)
+    g = torch.Generator(device=device).manual_seed(base + 6)
+    g_attn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
+    g_ffn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
+    # Cache contents of earlier tokens: N(0, 1), the rank's KV heads.
+    kfull = torch.randn(cfg.ctx, cfg.n_kv, cfg.head_dim, generator=g, device=device).half()
+    vfull = torch.randn(cfg.n_kv, cfg.head_dim // 8, cfg.ctx, 8, generator=g, device=device).half()
+    k0, k1 = plan.kv_heads
+    kcache = kfull[:, k0:k1].contiguous()
+    vcache = vfull[k0:k1].contiguous()
+    return LayerShard(qkv, o, gate, up, down, g_attn, g_ffn, kcache, vcache)
+
+
+@dataclass
+class Buffers:
+    x: torch.Tensor           # hidden state, full
+    x_mid: torch.Tensor       # x' (after attention block), full
+    qkv: torch.Tensor         # this rank's QKV rows
+    attn: torch.Tensor        # this rank's attention output
+    attn_full: torch.Tensor
+    o_slice: torch.Tensor
+    h: torch.Tensor
+    h_full: torch.Tensor
+    d_slice: torch.Tensor
+    ws: torch.Tensor          # attention workspace
+
+
+class ShardedDecoder:
+    """This rank's part of a `cfg.layers`-layer decoder.
+
+    `step(pos)` advances the hidden state `buf.x` by one token at position
+    `pos` (attending to tokens [0, pos]) and returns it.  With world > 1 the
+    all-gathers run through torch.distributed (NCCL) on the current stream, so
+    a step can be captured in a CUDA graph.
+    """
+
+    def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
+                 group=None, layers: list[LayerShard] | None = None):
+        self.cfg = cfg
+        self.plan = shard_plan(cfg, rank, world)
+        self.device = torch.device(device or "cuda")
+        self.group = group
+        self.layers = layers if layers is not None else [
+            build_layer(cfg, self.plan, i, self.device, seed) for i in range(cfg.layers)]
+        self.theta = rope_theta(cfg, self.device)
+        H, I, hd = cfg.hidden, cfg.inter, cfg.head_dim
+        p = self.plan
+        z = lambda n: torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.buf = Buffers(
+            x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd), attn_full=z(cfg.n_q * hd),
+            o_slice=z(p.o_rows[1] - p.o_rows[0]), h=z(p.ffn_rows[1] - p.ffn_rows[0]), h_full=z(I),
+            d_slice=z(p.o_rows[1] - p.o_rows[0]),
+            ws=ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device))
+
+    # -- bytes one step streams on this rank (weights, scales, KV cache, at ctx)
+    def step_bytes(self, pos: int) -> int:
+        cfg, p = self.cfg, self.plan
+        n = 0
+        for L in self.layers:
+            n += sum(w.nbytes for w in (L.qkv, L.o, L.gate, L.up, L.down))
+        kv = 2 * (pos + 1) * p.n_kv * cfg.head_dim * 2
+        return n + cfg.layers * kv
+
+    def _gather(self, out: torch.Tensor, part: torch.Tensor) -> None:
+        if self.plan.world == 1:
+            if out.data_ptr() != part.data_ptr():
+                out.copy_(part)
+            return
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(out, part, group=self.group)
+
+    def step(self, pos: int) -> torch.Tensor:
+        cfg, p, b = self.cfg, self.plan, self.buf
+        if not 0 <= pos < cfg.ctx:
+            raise ValueError(f"position {pos} outside the cache of {cfg.ctx} tokens")
+        hd = cfg.head_dim
+        q_rows, kv_rows = p.n_q * hd, p.n_kv * hd
+        o0, o1 = p.o_rows
+        scale = 1.0 / math.sqrt(hd)
+        single = p.world == 1
+        for L in self.layers:
+            ops.qkv_rope_append(L.qkv, b.x, L.g_attn, self.theta, pos, head_dim=hd, q_rows=q_rows, kv_rows=kv_rows,
+                                kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv)
+            ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
+                                 workspace=b.ws, out=b.attn_full if single else b.attn, ctx_cap=cfg.ctx)
+            if not single:
+                self._gather(b.attn_full, b.attn)
+            ops.gemv_residual(L.o, b.attn_full, b.x[o0:o1], out=b.x_mid if single else b.o_slice)
+            if not single:
+                self._gather(b.x_mid, b.o_slice)
+            ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h_full if single else b.h)
+            if not single:
+                self._gather(b.h_full, b.h)
+            ops.gemv_residual(L.down, b.h_full, b.x_mid[o0:o1], out=b.x if single else b.d_slice)
+            if not single:
+                self._gather(b.x, b.d_slice)
+        return b.x
+
+    def kernels_per_step(self) -> int:
+        return 5 * self.cfg.layers

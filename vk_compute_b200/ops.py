@@ -131,6 +131,25 @@ def gemv(w: PackedWeight, x: torch.Tensor, out=None, stream=None) -> torch.Tenso
     return y
 
 
+def gemv_residual(w: PackedWeight, x: torch.Tensor, residual: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    """y = W^T x + residual."""
+    y = _out(w.N, x, out)
+    check(lib().vkc_gemv_residual(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(residual), _p(y),
+                                  w.N, w.K, _s(stream)))
+    return y
+
+
+def qkv_rope_append(w: PackedWeight, x, gamma, theta, pos: int, *, head_dim: int, q_rows: int, kv_rows: int,
+                    kcache: torch.Tensor, vcache: torch.Tensor, ctx_cap: int, eps: float = 1e-6,
+                    rms_dim: int | None = None, out=None, stream=None) -> torch.Tensor:
+    """Fused QKV projection + RoPE + KV-cache append at token `pos`."""
+    y = _out(w.N, x, out)
+    check(lib().vkc_rmsnorm_gemv_rope_kv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma), _p(theta),
+                                         _p(y), w.N, w.K, eps, rms_dim or w.K, pos, head_dim, q_rows, kv_rows,
+                                         _p(kcache), _p(vcache), ctx_cap, _s(stream)))
+    return y
+
+
 def rmsnorm_gemv(w: PackedWeight, x, gamma, eps: float = 1e-6, rms_dim: int | None = None,
                  out=None, stream=None) -> torch.Tensor:
     y = _out(w.N, x, out)
@@ -167,14 +186,19 @@ def attention_workspace(n_q: int, n_kv: int, head_dim: int, ctx: int, device="cu
 
 def attention_decode(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx: int,
                      scale: float, workspace: torch.Tensor | None = None, out=None,
-                     stream=None) -> torch.Tensor:
-    """q [n_q*hd] fp16 or fp32; kcache fp16 [ctx][n_kv][hd];
-    vcache fp16 [n_kv][hd/8][ctx][8]."""
+                     stream=None, ctx_cap: int | None = None) -> torch.Tensor:
+    """q [n_q*hd] fp16 or fp32; kcache fp16 [cap][n_kv][hd];
+    vcache fp16 [n_kv][hd/8][cap][8] with cap = ctx_cap (default ctx);
+    attends tokens [0, ctx)."""
     o = _out(n_q * head_dim, q, out)
     qb = 32 if q.dtype == torch.float32 else 16
     ws_n = 0 if workspace is None else workspace.numel()
-    check(lib().vkc_attention_decode(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
-                                     scale, _p(workspace), ws_n, _s(stream)))
+    if ctx_cap is None:
+        check(lib().vkc_attention_decode(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
+                                         scale, _p(workspace), ws_n, _s(stream)))
+    else:
+        check(lib().vkc_attention_decode_cache(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
+                                               ctx_cap, scale, _p(workspace), ws_n, _s(stream)))
     return o
 
 
