@@ -366,8 +366,9 @@ void vko_swiglu(const float* x, const float* gamma, const float* wg, const float
  * shader: K token-major, K[t][kv][d] at (t*n_kv + kv)*hd + d (comp:55-59);
  * V in 8-dimension chunks per token, V[kv][d/8][t][d%8] (comp:69-73).  q is
  * fp16 [n_q][hd]; out is fp32 [n_q][hd].  Parity unpinned (no CPU check). */
-void vko_attention(const uint16_t* q, const uint16_t* kcache, const uint16_t* vcache, int n_q,
-                   int n_kv, int head_dim, int ctx, float scale, float* out) {
+static void attention_impl(const uint16_t* q16, const float* q32, const uint16_t* kcache,
+                           const uint16_t* vcache, int n_q, int n_kv, int head_dim, int ctx, float scale,
+                           float* out) {
     const int group = n_q / n_kv;
     double* sc = (double*)malloc(sizeof(double) * (size_t)ctx);
     for (int h = 0; h < n_q; ++h) {
@@ -376,9 +377,11 @@ void vko_attention(const uint16_t* q, const uint16_t* kcache, const uint16_t* vc
         for (int t = 0; t < ctx; ++t) {
             double s = 0.0;
             const uint16_t* kr = kcache + ((int64_t)t * n_kv + kv) * head_dim;
-            for (int d = 0; d < head_dim; ++d)
-                s += (double)vko_fp16_to_float(q[(int64_t)h * head_dim + d]) *
-                     vko_fp16_to_float(kr[d]);
+            for (int d = 0; d < head_dim; ++d) {
+                const int64_t qi = (int64_t)h * head_dim + d;
+                const double qv = q16 ? (double)vko_fp16_to_float(q16[qi]) : (double)q32[qi];
+                s += qv * vko_fp16_to_float(kr[d]);
+            }
             s *= scale;
             sc[t] = s;
             if (s > mx) mx = s;
@@ -396,6 +399,17 @@ void vko_attention(const uint16_t* q, const uint16_t* kcache, const uint16_t* vc
         }
     }
     free(sc);
+}
+
+void vko_attention(const uint16_t* q, const uint16_t* kcache, const uint16_t* vcache, int n_q,
+                   int n_kv, int head_dim, int ctx, float scale, float* out) {
+    attention_impl(q, NULL, kcache, vcache, n_q, n_kv, head_dim, ctx, scale, out);
+}
+
+/* The same with an fp32 query (the decode chain's QKV output is fp32). */
+void vko_attention_f32q(const float* q, const uint16_t* kcache, const uint16_t* vcache, int n_q,
+                        int n_kv, int head_dim, int ctx, float scale, float* out) {
+    attention_impl(NULL, q, kcache, vcache, n_q, n_kv, head_dim, ctx, scale, out);
 }
 
 /* shader/gemm.comp:19-59: C = A B, all row-major (A M x K, B K x N). */

@@ -58,6 +58,8 @@ void vko_swiglu(const float* x, const float* gamma, const float* wg, const float
                 int K, int N, int rms_dim, float eps, float* h);
 void vko_attention(const uint16_t* q, const uint16_t* kcache, const uint16_t* vcache,
                    int n_q, int n_kv, int head_dim, int ctx, float scale, float* out);
+void vko_attention_f32q(const float* q, const uint16_t* kcache, const uint16_t* vcache, int n_q,
+                        int n_kv, int head_dim, int ctx, float scale, float* out);
 void vko_gemm(const float* a, const float* b, int M, int N, int K, float* c);
 
 /* ---- the same operators on the reference's unpacked storage, threaded ----

@@ -50,6 +50,7 @@ def lib() -> C.CDLL:
             "vko_rope_pairs": (None, [_P, i, i, i, i, _P]),
             "vko_swiglu": (None, [_P, _P, _P, _P, i, i, i, f, _P]),
             "vko_attention": (None, [_P, _P, _P, i, i, i, i, f, _P]),
+            "vko_attention_f32q": (None, [_P, _P, _P, i, i, i, i, f, _P]),
             "vko_gemm": (None, [_P, _P, i, i, i, _P]),
             "vko_set_threads": (None, [i]),
             "vko_get_threads": (i, []),
@@ -173,6 +174,13 @@ def attention(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx: int, s
     out = np.empty(n_q * head_dim, np.float32)
     lib().vko_attention(_ptr(np.ascontiguousarray(q, np.uint16)), _ptr(np.ascontiguousarray(kcache, np.uint16)),
                         _ptr(np.ascontiguousarray(vcache, np.uint16)), n_q, n_kv, head_dim, ctx, scale, _ptr(out))
+    return out
+
+
+def attention_f32q(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx: int, scale: float) -> np.ndarray:
+    out = np.empty(n_q * head_dim, np.float32)
+    lib().vko_attention_f32q(_ptr(np.ascontiguousarray(q, np.float32)), _ptr(np.ascontiguousarray(kcache, np.uint16)),
+                             _ptr(np.ascontiguousarray(vcache, np.uint16)), n_q, n_kv, head_dim, ctx, scale, _ptr(out))
     return out
 
 

@@ -40,7 +40,8 @@ def test_config_shape(ctx):
     assert_close(out, ref, 2e-3, f"attention ctx={ctx}")
 
 
-@pytest.mark.parametrize("n_q,n_kv,hd", [(8, 8, 64), (16, 8, 128), (16, 4, 256), (4, 1, 128), (32, 8, 8)])
+@pytest.mark.parametrize("n_q,n_kv,hd", [(8, 8, 64), (16, 8, 128), (16, 4, 256), (4, 1, 128), (32, 8, 8),
+                                         (64, 8, 128), (8, 1, 256), (32, 4, 64), (16, 8, 32), (12, 3, 96)])
 def test_shapes(n_q, n_kv, hd):
     out, ref = run(n_q, n_kv, hd, 777, 1.0 / math.sqrt(hd))
     assert_close(out, ref, 2e-3, f"attention {n_q}/{n_kv}/{hd}")
@@ -55,6 +56,40 @@ def test_reference_scale_one():
 def test_fp32_query_and_library_workspace():
     out, ref = run(32, 8, 128, 4096, 1.0 / math.sqrt(128), q_fp32=True, workspace=False)
     assert_close(out, ref, 2e-3, "attention fp32 q")
+
+
+@pytest.mark.parametrize("n_q,n_kv,hd,ctx", [(32, 8, 128, 3001), (64, 8, 128, 515), (16, 4, 256, 1500),
+                                              (8, 2, 64, 4097)])
+def test_fp32_query_full_precision(n_q, n_kv, hd, ctx):
+    """fp32 q values that fp16 cannot hold (the decode chain's QKV output)."""
+    _, k, v = make_cache(n_q, n_kv, hd, ctx, seed=5)
+    g = torch.Generator().manual_seed(6)
+    q = torch.randn(n_q * hd, generator=g) * 1.7
+    ref = o.attention_f32q(q.numpy(), k.numpy().view(np.uint16), v.numpy().view(np.uint16), n_q, n_kv, hd, ctx,
+                           1.0 / math.sqrt(hd))
+    out = ops.attention_decode(q.cuda(), k.cuda(), v.cuda(), n_q, n_kv, hd, ctx, 1.0 / math.sqrt(hd))
+    assert_close(out.cpu().numpy(), ref, 2e-3, f"attention fp32 q {n_q}/{n_kv}/{hd}/{ctx}")
+
+
+def test_peaked_scores():
+    """Large scores (scale 1, |q| ~ 4): the softmax is dominated by a few tokens,
+    so the running maximum changes between sub-tiles and splits."""
+    n_q, n_kv, hd, ctx = 32, 8, 128, 2500
+    _, k, v = make_cache(n_q, n_kv, hd, ctx, seed=7)
+    g = torch.Generator().manual_seed(8)
+    q = torch.randn(n_q * hd, generator=g) * 4.0
+    ref = o.attention_f32q(q.numpy(), k.numpy().view(np.uint16), v.numpy().view(np.uint16), n_q, n_kv, hd, ctx, 0.25)
+    out = ops.attention_decode(q.cuda(), k.cuda(), v.cuda(), n_q, n_kv, hd, ctx, 0.25)
+    assert_close(out.cpu().numpy(), ref, 2e-3, "attention peaked")
+
+
+def test_unsupported_group_rejected():
+    from vk_compute_b200._lib import VkcError
+    q = torch.zeros(16 * 8, dtype=torch.float16, device="cuda")
+    k = torch.zeros(4, 1, 8, dtype=torch.float16, device="cuda")
+    v = torch.zeros(1, 1, 4, 8, dtype=torch.float16, device="cuda")
+    with pytest.raises(VkcError, match="query heads per KV head 16"):
+        ops.attention_decode(q, k, v, 16, 1, 8, 4, 1.0)
 
 
 def test_repeated_calls_reuse_workspace():

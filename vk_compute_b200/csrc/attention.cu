@@ -10,28 +10,32 @@
 // Cache layouts are the shader's: K token-major, K[t][kv][d] at
 // (t*n_kv + kv)*hd + d (comp:55-59); V in 8-dimension chunks, 16 bytes per
 // token, V[kv][d/8][t][d%8] (comp:69-73), so for one head and one chunk the
-// tokens are a contiguous 16-byte stream.
+// tokens are a contiguous 16-byte stream.  A cache allocated for ctx_cap
+// tokens has V runs ctx_cap long.
 //
-// Decomposition (split-KV): CTA (split, kv) owns T consecutive tokens of one
-// KV head and serves all G query heads of that head, so every K and V byte is
-// read once.  Phase 1: lanes split a K row into 16-byte chunks and reduce the
-// partial dots over the row's lanes.  Phase 2: per-head max and exponentials
-// in shared memory.  Phase 3: warps take V dimension chunks, lanes take tokens
-// (512 contiguous bytes per warp load), and a butterfly transpose-reduction
-// leaves lane l with output (head, dim) pair l.  Each CTA writes its (max,
-// sum, unnormalised output) to a workspace; the last CTA of a KV head to
-// finish (atomic ticket) merges the splits and resets the ticket.
+// Decomposition (split-KV, flash-decoding): CTA (split, kv) owns a range of
+// tokens of one KV head and serves all G query heads of that head, so every K
+// and V byte is read once.  The range streams through a three-stage ring of
+// (K, V) sub-tiles in shared memory filled by 16-byte cp.async copies (zero
+// fill past the end), issued two sub-tiles ahead.  Per sub-tile: lanes split a
+// K row into 16-byte chunks and reduce the partial dots; one warp per head
+// updates the running maximum and sum (base-2 online softmax) and rescales;
+// threads own one output dimension for all G heads and a share of the tokens
+// for P.V.  Each CTA writes (max, sum, unnormalised output) to a workspace;
+// the last CTA of a KV head to finish (atomic ticket) merges the splits in
+// split order and resets the ticket.
 #include "vkc_common.cuh"
 
 #include <cuda_fp16.h>
 
 #include <mutex>
-
+#include <type_traits>
 
 namespace vkc {
 namespace {
 
 constexpr int kAttThreads = 256;
+constexpr int kAttStages = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnParams {
@@ -44,226 +48,662 @@ struct AttnParams {
     unsigned* tickets;  // [n_kv]
     int n_q, n_kv, hd, ctx, splits, tpc;
     int ctx_cap;        // V run length per (head, chunk): the cache capacity
+    int tt;             // tokens per sub-tile (a multiple of 32)
     float scale_log2;   // scale * log2(e)
 };
 
-__device__ __forceinline__ void half8_to_float(const uint4 c, float (&v)[8]) {
-    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-    }
+// One ring stage in 16-byte units: K sub-tile [tt][chunks], then the V
+// sub-tile [chunks][tt + 1] (one unit of padding per run makes the P.V reads,
+// lanes over 8 chunks of one token, hit 32 distinct banks).
+__host__ __device__ __forceinline__ int att_v_stride(int tt) { return tt + 1; }
+__host__ __device__ __forceinline__ int att_stage_units(int tt, int chunks) {
+    return tt * chunks + chunks * att_v_stride(tt);
 }
 
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// Sums G per-lane values over the `lpt` lanes of a row group (lpt a power of
+// two >= G) by halving exchanges: each level trades half of the remaining
+// values with the partner lane, so G heads cost log2(lpt) + G - 1 shuffles
+// instead of G log2(lpt).  Returns the total of head `g` (set on return).
 template <int G>
-__global__ void __launch_bounds__(kAttThreads) attention_decode_kernel(const AttnParams p) {
-    extern __shared__ float sc[];  // [G][tpc] scores, then probabilities
-    __shared__ float stat[G][2];   // per head: max, sum
-    __shared__ float wred[kAttThreads / 32][G];
+__device__ __forceinline__ float reduce_heads(float (&v)[G], int lane, int lpt, int& g) {
+    int m = lpt >> 1;
+    g = 0;
+    if constexpr (G == 4) {
+        const bool up = lane & m;
+        const float s0 = up ? v[0] : v[2], s1 = up ? v[1] : v[3];
+        const float k0 = up ? v[2] : v[0], k1 = up ? v[3] : v[1];
+        v[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, m);
+        v[1] = k1 + __shfl_xor_sync(0xffffffffu, s1, m);
+        g = up ? 2 : 0;
+        m >>= 1;
+    }
+    if constexpr (G >= 2) {
+        const bool up = lane & m;
+        const float s0 = up ? v[0] : v[1], k0 = up ? v[1] : v[0];
+        v[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, m);
+        g += up ? 1 : 0;
+        m >>= 1;
+    }
+    float r = v[0];
+    for (; m >= 1; m >>= 1) r += __shfl_xor_sync(0xffffffffu, r, m);
+    return r;
+}
+
+// The last CTA of KV head `kv` to finish (atomic ticket) merges the splits of
+// its G query heads in split order and resets the ticket for the next launch.
+// Split weights w[g][s] = 2^(m_s - max) / sum_s 2^(m_s - max) l_s go to `smem`
+// (free by now); out = sum_s w[g][s] acc_s.
+template <int G>
+__device__ __forceinline__ void merge_splits(const AttnParams& p, uint8_t* smem, int kv) {
     __shared__ unsigned s_ticket;
-
-    const int split = blockIdx.x, kv = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hd = p.hd, chunks = hd / 8;
-    const int t0 = split * p.tpc;
-    const int T = min(p.tpc, p.ctx - t0);
-    const int h0 = kv * G;
-
-    pdl_launch_dependents();
-    pdl_wait();
-
-    // ---- phase 1: scores ----------------------------------------------------
-    // A K row of hd halves is `chunks` 16-byte pieces; `lpt` lanes share a row.
-    int lpt = 1;
-    while (lpt < chunks) lpt <<= 1;  // power of two >= chunks, <= 32
-    const int rows_per_warp = 32 / lpt;
-    const int sub = lane % lpt, row_in_warp = lane / lpt;
-    float qv[G][8];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        if (sub >= chunks) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qv[g][i] = 0.f;
-        } else if (p.q_bits == 16) {
-            const uint4 qc = reinterpret_cast<const uint4*>(p.q)[((h0 + g) * hd) / 8 + sub];
-            half8_to_float(qc, qv[g]);
-        } else {
-            const float4* q4 = reinterpret_cast<const float4*>(p.q) + ((h0 + g) * hd) / 4 + 2 * sub;
-            const float4 a = q4[0], b = q4[1];
-            qv[g][0] = a.x; qv[g][1] = a.y; qv[g][2] = a.z; qv[g][3] = a.w;
-            qv[g][4] = b.x; qv[g][5] = b.y; qv[g][6] = b.z; qv[g][7] = b.w;
-        }
-    }
-    const size_t krow = static_cast<size_t>(p.n_kv) * chunks;  // uint4 per token
-    const int step = (kAttThreads / 32) * rows_per_warp;
-    for (int tb = warp * rows_per_warp; tb < T; tb += step * 4) {
-        uint4 kc[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int t = tb + u * step + row_in_warp;
-            kc[u] = (t < T && sub < chunks)
-                        ? ld_stream(p.kc + static_cast<size_t>(t0 + t) * krow + kv * chunks + sub)
-                        : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            float kf[8];
-            half8_to_float(kc[u], kf);
-            float d[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float a = 0.f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a = fmaf(qv[g][i], kf[i], a);
-                d[g] = a;
-            }
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1)
-                if (o < lpt)
-#pragma unroll
-                    for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
-            const int t = tb + u * step + row_in_warp;
-            if (sub == 0 && t < T)
-#pragma unroll
-                for (int g = 0; g < G; ++g) sc[g * p.tpc + t] = d[g] * p.scale_log2;
-        }
-    }
-    __syncthreads();
-
-    // ---- phase 2: softmax statistics (base 2) -------------------------------
-    float mx[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
-    for (int t = tid; t < T; t += kAttThreads)
-#pragma unroll
-        for (int g = 0; g < G; ++g) mx[g] = fmaxf(mx[g], sc[g * p.tpc + t]);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], o));
-        if (lane == 0) wred[warp][g] = mx[g];
-    }
-    __syncthreads();
-    if (tid < G) {
-        float m = -INFINITY;
-        for (int w = 0; w < kAttThreads / 32; ++w) m = fmaxf(m, wred[w][tid]);
-        stat[tid][0] = m;
-    }
-    __syncthreads();
-    float sm[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) sm[g] = 0.f;
-    for (int t = tid; t < T; t += kAttThreads)
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float e = exp2f(sc[g * p.tpc + t] - stat[g][0]);
-            sc[g * p.tpc + t] = e;
-            sm[g] += e;
-        }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        sm[g] = warp_sum(sm[g]);
-        if (lane == 0) wred[warp][g] = sm[g];
-    }
-    __syncthreads();
-    if (tid < G) {
-        float s = 0.f;
-        for (int w = 0; w < kAttThreads / 32; ++w) s += wred[w][tid];
-        stat[tid][1] = s;
-    }
-    __syncthreads();
-
-    // ---- phase 3: probabilities x V ------------------------------------------
-    const size_t vrun = static_cast<size_t>(p.ctx_cap);  // uint4 per (kv, chunk) run
-    for (int c = warp; c < chunks; c += kAttThreads / 32) {
-        float acc[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-        const uint4* vbase = p.vc + (static_cast<size_t>(kv) * chunks + c) * vrun + t0;
-        for (int tb = 0; tb < T; tb += 32 * 4) {
-            uint4 vchunk[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int t = tb + u * 32 + lane;
-                vchunk[u] = t < T ? ld_stream(vbase + t) : make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int t = tb + u * 32 + lane;
-                float vf[8];
-                half8_to_float(vchunk[u], vf);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float pr = t < T ? sc[g * p.tpc + t] : 0.f;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) acc[g * 8 + i] = fmaf(pr, vf[i], acc[g * 8 + i]);
-                }
-            }
-        }
-        // Butterfly transpose-reduction: lane l ends with the total of acc[l].
-#pragma unroll
-        for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < n / 2; ++i) {
-                const float send = upper ? acc[i] : acc[i + n / 2];
-                const float keep = upper ? acc[i + n / 2] : acc[i];
-                acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        const int g = lane / 8, i = lane % 8;
-        if (g < G) {
-            const int h = h0 + g;
-            p.ws[(static_cast<size_t>(h) * p.splits + split) * (hd + 2) + c * 8 + i] = acc[0];
-        }
-    }
-    if (tid < G) {
-        float* rec = p.ws + (static_cast<size_t>(h0 + tid) * p.splits + split) * (hd + 2) + hd;
-        rec[0] = stat[tid][0];
-        rec[1] = stat[tid][1];
-    }
-
-    // ---- merge: the last split of this KV head combines all splits ----------
+    const int hd = p.hd, h0 = kv * G;
     __threadfence();
     __syncthreads();
     if (tid == 0) s_ticket = atomicAdd(p.tickets + kv, 1u);
     __syncthreads();
     if (s_ticket != static_cast<unsigned>(p.splits - 1)) return;
     __threadfence();
-    for (int e = tid; e < G * hd; e += kAttThreads) {
-        const int g = e / hd, d = e % hd, h = h0 + g;
-        const float* base = p.ws + static_cast<size_t>(h) * p.splits * (hd + 2);
+    float* wts = reinterpret_cast<float*>(smem);  // [G][splits]
+    for (int i = tid; i < G * p.splits; i += kAttThreads) {
+        const int g = i / p.splits, s2 = i - g * p.splits;
+        wts[i] = __ldcg(p.ws + (static_cast<size_t>(h0 + g) * p.splits + s2) * (hd + 2) + hd);
+    }
+    __syncthreads();
+    if (warp < G) {
+        const int g = warp;
+        const float* rb = p.ws + static_cast<size_t>(h0 + g) * p.splits * (hd + 2) + hd;
         float m = -INFINITY;
-        for (int s = 0; s < p.splits; ++s) m = fmaxf(m, __ldcg(base + s * (hd + 2) + hd));
-        float num = 0.f, den = 0.f;
-        for (int s = 0; s < p.splits; ++s) {
-            const float* r = base + s * (hd + 2);
-            const float w = exp2f(__ldcg(r + hd) - m);
-            num = fmaf(w, __ldcg(r + d), num);
-            den = fmaf(w, __ldcg(r + hd + 1), den);
+        for (int s2 = lane; s2 < p.splits; s2 += 32) m = fmaxf(m, wts[g * p.splits + s2]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float den = 0.f;
+        for (int s2 = lane; s2 < p.splits; s2 += 32) {
+            const float w = exp2f(wts[g * p.splits + s2] - m);
+            wts[g * p.splits + s2] = w;
+            den = fmaf(w, __ldcg(rb + s2 * (hd + 2) + 1), den);
         }
-        p.out[static_cast<size_t>(h) * hd + d] = num / den;
+        den = warp_sum(den);
+        const float inv = 1.f / den;
+        __syncwarp();
+        for (int s2 = lane; s2 < p.splits; s2 += 32) wts[g * p.splits + s2] *= inv;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hd; i += kAttThreads) {
+        const int g = i / hd, d = i - g * hd;
+        const float* rb = p.ws + static_cast<size_t>(h0 + g) * p.splits * (hd + 2) + d;
+        const float* w = wts + g * p.splits;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int s2 = 0;
+        for (; s2 + 4 <= p.splits; s2 += 4) {
+            a0 = fmaf(w[s2], __ldcg(rb + (s2) * (hd + 2)), a0);
+            a1 = fmaf(w[s2 + 1], __ldcg(rb + (s2 + 1) * (hd + 2)), a1);
+            a2 = fmaf(w[s2 + 2], __ldcg(rb + (s2 + 2) * (hd + 2)), a2);
+            a3 = fmaf(w[s2 + 3], __ldcg(rb + (s2 + 3) * (hd + 2)), a3);
+        }
+        for (; s2 < p.splits; ++s2) a0 = fmaf(w[s2], __ldcg(rb + s2 * (hd + 2)), a0);
+        p.out[static_cast<size_t>(h0 + g) * hd + d] = (a0 + a1) + (a2 + a3);
     }
     if (tid == 0) p.tickets[kv] = 0u;
 }
 
+template <int G>
+__global__ void __launch_bounds__(kAttThreads, 2) attention_decode_kernel(const AttnParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_m[G], s_l[G], s_f[G];
+
+    const int split = blockIdx.x, kv = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hd = p.hd, chunks = hd / 8, TT = p.tt;
+    const int t0 = split * p.tpc;
+    const int T = min(p.tpc, p.ctx - t0);
+    const int nsub = (T + TT - 1) / TT;
+    const int h0 = kv * G;
+    const int k_units = TT * chunks, vstride = att_v_stride(TT);
+    const int stage_units = att_stage_units(TT, chunks);
+    uint4* ring = reinterpret_cast<uint4*>(smem);
+    float* qs = reinterpret_cast<float*>(smem + static_cast<size_t>(kAttStages) * stage_units * 16);  // [G][hd]
+    float* sc = qs + G * hd;                                                                          // [G][TT]
+
+    pdl_launch_dependents();
+    // The cache row of the current token and q may come from the previous kernel.
+    pdl_wait();
+
+    auto issue = [&](int s) {
+        uint4* base = ring + (s % kAttStages) * stage_units;
+        const int ts = t0 + s * TT;
+        const int nt = min(TT, T - s * TT);
+        for (int u = tid; u < TT * chunks; u += kAttThreads) {
+            const int t = u / chunks, c = u - t * chunks;
+            const bool ok = t < nt;
+            const uint4* src = p.kc + (static_cast<size_t>(ok ? ts + t : t0) * p.n_kv + kv) * chunks + c;
+            cp_async16_zfill(smem_addr(base + u), src, ok);
+        }
+        for (int u = tid; u < TT * chunks; u += kAttThreads) {
+            const int c = u / TT, t = u - c * TT;
+            const bool ok = t < nt;
+            const uint4* src = p.vc + (static_cast<size_t>(kv) * chunks + c) * p.ctx_cap + (ok ? ts + t : t0);
+            cp_async16_zfill(smem_addr(base + k_units + c * vstride + t), src, ok);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < kAttStages - 1; ++s) {
+        if (s < nsub) issue(s);
+        cp_commit();
+    }
+
+    for (int i = tid; i < G * hd; i += kAttThreads) {
+        const int g = i / hd, d = i - g * hd;
+        const size_t qi = static_cast<size_t>(h0 + g) * hd + d;
+        qs[i] = p.q_bits == 16 ? __half2float(reinterpret_cast<const __half*>(p.q)[qi])
+                               : reinterpret_cast<const float*>(p.q)[qi];
+    }
+    if (tid < G) {
+        s_m[tid] = -INFINITY;
+        s_l[tid] = 0.f;
+    }
+    __syncthreads();
+
+    // Score mapping: `lpt` lanes (a power of two >= chunks) share a K row;
+    // lane `sub` owns dimensions [8 sub, 8 sub + 8) and keeps q for them.
+    int lpt = 1;
+    while (lpt < chunks) lpt <<= 1;
+    const int rpw = 32 / lpt;
+    const int sub = lane & (lpt - 1), rw = lane / lpt;
+    const bool split_heads = lpt >= G;
+    float qr[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qr[g][i] = sub < chunks ? qs[g * hd + sub * 8 + i] : 0.f;
+
+    // P.V mapping: thread owns dimensions (2 dp, 2 dp + 1) of every head and
+    // tokens [tg * per, tg * per + per) of each sub-tile.
+    const int pairs = hd / 2, ntg = kAttThreads / pairs;
+    const int dp = tid % pairs, tg = tid / pairs;
+    const bool pv = tg < ntg;
+    const int per = (((TT + ntg - 1) / ntg) + 3) & ~3;
+    const int lo = min(tg * per, TT), hi = min(lo + per, TT);
+    const int vc_word = (dp >> 2) * vstride * 4 + (dp & 3);  // 32-bit word of (chunk, token 0)
+    float acc[G][2];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = 0.f;
+
+    for (int s = 0; s < nsub; ++s) {
+        cp_wait<kAttStages - 2>();
+        __syncthreads();  // sub-tile s landed for all; sub-tile s-1 fully consumed
+        if (s + kAttStages - 1 < nsub) issue(s + kAttStages - 1);
+        cp_commit();
+        const uint4* base = ring + (s % kAttStages) * stage_units;
+        const int nt = min(TT, T - s * TT);
+
+        // (a) scores in base 2, -inf past the end of the range
+        for (int tb = 0; tb < TT; tb += (kAttThreads / 32) * rpw) {
+            const int t = tb + warp * rpw + rw;
+            const bool row = t < TT;
+            float dots[G];
+            if (row && sub < chunks) {
+                const uint4 kq = base[t * chunks + sub];
+                const float2 k0 = half2_bits_to_float2(kq.x), k1 = half2_bits_to_float2(kq.y);
+                const float2 k2 = half2_bits_to_float2(kq.z), k3 = half2_bits_to_float2(kq.w);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float a = qr[g][0] * k0.x;
+                    a = fmaf(qr[g][1], k0.y, a);
+                    a = fmaf(qr[g][2], k1.x, a);
+                    a = fmaf(qr[g][3], k1.y, a);
+                    a = fmaf(qr[g][4], k2.x, a);
+                    a = fmaf(qr[g][5], k2.y, a);
+                    a = fmaf(qr[g][6], k3.x, a);
+                    a = fmaf(qr[g][7], k3.y, a);
+                    dots[g] = a;
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < G; ++g) dots[g] = 0.f;
+            }
+            if (split_heads) {
+                int g;
+                const float r = reduce_heads<G>(dots, lane, lpt, g);
+                if (row && (sub & (lpt / G - 1)) == 0) sc[g * TT + t] = t < nt ? r * p.scale_log2 : -INFINITY;
+            } else {
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1)
+                    if (o < lpt)
+#pragma unroll
+                        for (int g = 0; g < G; ++g) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], o);
+                if (row && sub == 0)
+#pragma unroll
+                    for (int g = 0; g < G; ++g) sc[g * TT + t] = t < nt ? dots[g] * p.scale_log2 : -INFINITY;
+            }
+        }
+        __syncthreads();
+
+        // (b) online softmax, one warp per head
+        if (warp < G) {
+            const int g = warp;
+            float mx = -INFINITY;
+            for (int t = lane; t < TT; t += 32) mx = fmaxf(mx, sc[g * TT + t]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float m_old = s_m[g];
+            const float m_new = fmaxf(m_old, mx);
+            float sum = 0.f;
+            for (int t = lane; t < TT; t += 32) {
+                const float e = exp2f(sc[g * TT + t] - m_new);
+                sc[g * TT + t] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float f = exp2f(m_old - m_new);
+                s_m[g] = m_new;
+                s_l[g] = s_l[g] * f + sum;
+                s_f[g] = f;
+            }
+        }
+        __syncthreads();
+
+        // (c) P.V over this thread's tokens (zero V and zero weight past the end)
+        if (pv) {
+            const uint32_t* vw = reinterpret_cast<const uint32_t*>(base + k_units) + vc_word;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float f = s_f[g];
+                acc[g][0] *= f;
+                acc[g][1] *= f;
+            }
+            for (int t = lo; t < hi; t += 4) {
+                float4 pg[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) pg[g] = *reinterpret_cast<const float4*>(sc + g * TT + t);
+                float2 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = half2_bits_to_float2(vw[(t + u) * 4]);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    acc[g][0] = fmaf(pg[g].x, v[0].x, acc[g][0]);
+                    acc[g][1] = fmaf(pg[g].x, v[0].y, acc[g][1]);
+                    acc[g][0] = fmaf(pg[g].y, v[1].x, acc[g][0]);
+                    acc[g][1] = fmaf(pg[g].y, v[1].y, acc[g][1]);
+                    acc[g][0] = fmaf(pg[g].z, v[2].x, acc[g][0]);
+                    acc[g][1] = fmaf(pg[g].z, v[2].y, acc[g][1]);
+                    acc[g][0] = fmaf(pg[g].w, v[3].x, acc[g][0]);
+                    acc[g][1] = fmaf(pg[g].w, v[3].y, acc[g][1]);
+                }
+            }
+        }
+    }
+    cp_wait<0>();
+    __syncthreads();
+
+    // Combine token groups (the ring is free now) and write the partial.
+    float* red = reinterpret_cast<float*>(smem);  // [ntg][G][hd]
+    if (pv)
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            *reinterpret_cast<float2*>(red + (tg * G + g) * hd + 2 * dp) = make_float2(acc[g][0], acc[g][1]);
+    __syncthreads();
+    for (int i = tid; i < G * hd; i += kAttThreads) {
+        const int g = i / hd, d = i - g * hd;
+        float v = 0.f;
+        for (int q = 0; q < ntg; ++q) v += red[(q * G + g) * hd + d];
+        p.ws[(static_cast<size_t>(h0 + g) * p.splits + split) * (hd + 2) + d] = v;
+    }
+    if (tid < G) {
+        float* rec = p.ws + (static_cast<size_t>(h0 + tid) * p.splits + split) * (hd + 2) + hd;
+        rec[0] = s_m[tid];
+        rec[1] = s_l[tid];
+    }
+
+    merge_splits<G>(p, smem, kv);
+}
+
+// ---- tensor-core variant (head_dim 64 / 128 / 256) ---------------------------
+//
+// Same decomposition and ring; the two contractions run on mma.sync
+// m16n8k16 (f16 inputs, f32 accumulation) with the G query heads as the rows
+// of A (rows G..15 zero).  q and p are fp32: each is split into fp16 high and
+// low parts (x = hi + lo, |lo| <= 2^-11 |x|) and both parts are multiplied, so
+// the products carry about 22 significant bits, as fp32 FMAs would; K and V
+// are fp16 already.  For a decode step (G <= 8 rows) the tensor cores only
+// remove issue pressure: the per-token work drops from ~40 instructions to a
+// few, leaving the kernel bound by the cache stream.
+//
+//   scores   C[g][t]  = sum_d q[g][d] K[t][d]   B = K sub-tile, ldmatrix (rows = tokens)
+//   P.V      O[g][d] += sum_t p[g][t] V[t][d]   B = V sub-tile, ldmatrix.trans (rows = tokens)
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    // Rows 8..15 of A are zero (at most eight query heads per KV head).
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// fp16 high/low split of a pair of fp32 values.
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = h2_bits(h);
+    lo = h2_bits(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+
+template <int HD>
+struct MmaGeo {
+    static constexpr int CH = HD / 8;              // 16-byte chunks per K row
+    static constexpr int TT = 8192 / HD;           // tokens per sub-tile (32 KB of K + V)
+    static constexpr int KROW = CH + 1;            // K row pitch (units), padded
+    static constexpr int VROW = TT + 1;            // V run pitch (units), padded
+    static constexpr int KU = TT * KROW;
+    static constexpr int SU = KU + CH * VROW;      // units per ring stage
+    static constexpr int NT = TT / 8;              // token tiles (scores n-tiles)
+    static constexpr int KG = NT >= 8 ? 1 : 8 / NT;          // warps sharing a token tile
+    static constexpr int TPW = NT >= 8 ? NT / 8 : 1;         // token tiles per warp
+    static constexpr int KS = HD / 16 / KG;                  // score k-steps per warp
+    static constexpr int NP = HD / 16;             // pairs of 8-dimension n-tiles
+    static constexpr int WN = NP < 8 ? NP : 8;     // warps along dimensions
+    static constexpr int WK = 8 / WN;              // warps along tokens
+    static constexpr int PPW = NP / WN;            // dimension pairs per warp
+    static constexpr int PKS = TT / 16 / WK;       // P.V k-steps per warp
+    static constexpr int PROW = TT + 8;            // halves per P row (conflict-free A loads)
+    static constexpr size_t ring_bytes = static_cast<size_t>(kAttStages) * SU * 16;
+    static constexpr size_t sc_bytes = static_cast<size_t>(KG) * 8 * TT * sizeof(float);
+    static constexpr size_t p_bytes = 2ull * 8 * PROW * sizeof(__half);
+    static constexpr size_t q_bytes = static_cast<size_t>(HD / 16) * 32 * 16;
+    static constexpr size_t smem_bytes = ring_bytes + sc_bytes + p_bytes + q_bytes;
+    static_assert(KS % 2 == 0 && NT * KG >= 8 && WN * WK == 8 && PKS >= 1, "geometry");
+};
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const AttnParams p) {
+    using Geo = MmaGeo<HD>;
+    constexpr int CH = Geo::CH, TT = Geo::TT, KROW = Geo::KROW, VROW = Geo::VROW, KU = Geo::KU, SU = Geo::SU;
+    constexpr int NT = Geo::NT, KG = Geo::KG, TPW = Geo::TPW, KS = Geo::KS;
+    constexpr int WN = Geo::WN, WK = Geo::WK, PPW = Geo::PPW, PKS = Geo::PKS, PROW = Geo::PROW;
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_m[G], s_l[G], s_f[G];
+
+    const int split = blockIdx.x, kv = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gid = lane >> 2, t4 = lane & 3;
+    const int t0 = split * p.tpc;
+    const int T = min(p.tpc, p.ctx - t0);
+    const int nsub = (T + TT - 1) / TT;
+    const int h0 = kv * G;
+    uint4* ring = reinterpret_cast<uint4*>(smem);
+    float* sc = reinterpret_cast<float*>(smem + Geo::ring_bytes);                      // [KG][8][TT]
+    __half* ph = reinterpret_cast<__half*>(smem + Geo::ring_bytes + Geo::sc_bytes);    // [8][PROW]
+    __half* pl = ph + 8 * PROW;
+    uint4* qf = reinterpret_cast<uint4*>(smem + Geo::ring_bytes + Geo::sc_bytes + Geo::p_bytes);  // [HD/16][32]
+    const int kgi = KG == 1 ? 0 : warp / NT;  // this warp's k-range for scores
+
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // Copy plan: 1024 K units and 1024 V units per sub-tile, four of each per
+    // thread.  K: chunk tid % CH of tokens tid / CH + i (256 / CH).  V: token
+    // tid % TT of chunks tid / TT + i (256 / TT).
+    const int k_tok = tid / CH, k_chk = tid % CH;
+    const int v_tok = tid % TT, v_chk = tid / TT;
+    const uint4* k_src0 = p.kc + (static_cast<size_t>(t0 + k_tok) * p.n_kv + kv) * CH + k_chk;
+    const size_t k_step = static_cast<size_t>(256 / CH) * p.n_kv * CH;
+    const uint4* v_src0 = p.vc + (static_cast<size_t>(kv) * CH + v_chk) * p.ctx_cap + t0 + v_tok;
+    const size_t v_step = static_cast<size_t>(256 / TT) * p.ctx_cap;
+    const int k_dst0 = k_tok * KROW + k_chk, v_dst0 = KU + v_chk * VROW + v_tok;
+    auto issue = [&](int s) {
+        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const int nt = min(TT, T - s * TT);
+        const size_t tok = static_cast<size_t>(s) * TT;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int t = k_tok + i * (256 / CH);
+            const bool ok = t < nt;
+            const uint4* src = ok ? k_src0 + tok * p.n_kv * CH + i * k_step : p.kc;
+            cp_async16_zfill(base + (k_dst0 + i * (256 / CH) * KROW) * 16, src, ok);
+        }
+        const bool vok = v_tok < nt;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4* src = vok ? v_src0 + tok + i * v_step : p.vc;
+            cp_async16_zfill(base + (v_dst0 + i * (256 / TT) * VROW) * 16, src, vok);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < kAttStages - 1; ++s) {
+        if (s < nsub) issue(s);
+        cp_commit();
+    }
+
+    // q as A fragments (rows = heads) in shared memory, split into fp16 high
+    // and low parts: entry (k-step, lane) = {hi R0, hi R2, lo R0, lo R2}.
+    for (int e = tid; e < (HD / 16) * 32; e += kAttThreads) {
+        const int kj = e >> 5, g = (e & 31) >> 2, q4 = e & 3;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (g < G) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const size_t qi = static_cast<size_t>(h0 + g) * HD + kj * 16 + half * 8 + 2 * q4;
+                float2 f;
+                if (p.q_bits == 16)
+                    f = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(p.q) + qi));
+                else
+                    f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(p.q) + qi);
+                x[2 * half] = f.x;
+                x[2 * half + 1] = f.y;
+            }
+        }
+        uint4 fr;
+        split_pair(x[0], x[1], fr.x, fr.z);
+        split_pair(x[2], x[3], fr.y, fr.w);
+        qf[e] = fr;
+    }
+    const bool q_lo = p.q_bits != 16;  // fp16 q has no low part
+    if (tid < G) {
+        s_m[tid] = -INFINITY;
+        s_l[tid] = 0.f;
+    }
+
+    float acc[PPW][2][4];
+#pragma unroll
+    for (int j = 0; j < PPW; ++j)
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][n][i] = 0.f;
+    const int pw = warp % WN, pk = warp / WN;  // P.V: dimension pairs pw + WN j, k-steps of group pk
+
+    for (int s = 0; s < nsub; ++s) {
+        cp_wait<kAttStages - 2>();
+        __syncthreads();  // sub-tile s landed for all; sub-tile s-1 fully consumed
+        if (s + kAttStages - 1 < nsub) issue(s + kAttStages - 1);
+        cp_commit();
+        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const int nt = min(TT, T - s * TT);
+
+        // (a) raw scores of this warp's token tiles (partial over k when KG > 1)
+#pragma unroll
+        for (int j = 0; j < TPW; ++j) {
+            const int tile = KG == 1 ? warp + 8 * j : warp % NT;
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            const int tok = tile * 8 + (lane & 7);
+#pragma unroll
+            for (int ks = 0; ks < KS; ks += 2) {
+                const int chunk = (kgi * KS + ks) * 2 + (lane >> 3);
+                uint32_t b[4];
+                ldsm_x4(base + (tok * KROW + chunk) * 16, b);
+                const uint4 qa = qf[(kgi * KS + ks) * 32 + lane], qb = qf[(kgi * KS + ks + 1) * 32 + lane];
+                mma16816(c, qa.x, qa.y, b[0], b[1]);
+                mma16816(c, qb.x, qb.y, b[2], b[3]);
+                if (q_lo) {
+                    mma16816(c, qa.z, qa.w, b[0], b[1]);
+                    mma16816(c, qb.z, qb.w, b[2], b[3]);
+                }
+            }
+            if (gid < G)
+                *reinterpret_cast<float2*>(sc + (kgi * 8 + gid) * TT + tile * 8 + 2 * t4) = make_float2(c[0], c[1]);
+        }
+        __syncthreads();
+
+        // (b) online softmax, one warp per head; p split into fp16 hi / lo
+        if (warp < G) {
+            const int g = warp;
+            float v[TT / 32];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < TT / 32; ++i) {
+                const int t = lane + 32 * i;
+                float x = 0.f;
+#pragma unroll
+                for (int k = 0; k < KG; ++k) x += sc[(k * 8 + g) * TT + t];
+                v[i] = t < nt ? x * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, v[i]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float m_old = s_m[g];
+            const float m_new = fmaxf(m_old, mx);
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < TT / 32; ++i) {
+                const int t = lane + 32 * i;
+                const float e = exp2f(v[i] - m_new);
+                const __half eh = __float2half_rn(e);
+                ph[g * PROW + t] = eh;
+                pl[g * PROW + t] = __float2half_rn(e - __half2float(eh));
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float f = exp2f(m_old - m_new);
+                s_m[g] = m_new;
+                s_l[g] = s_l[g] * f + sum;
+                s_f[g] = f;
+            }
+        }
+        __syncthreads();
+
+        // (c) P.V for this warp's dimension pairs and token k-steps
+        const bool row = gid < G;
+        const float f = row ? s_f[gid] : 0.f;
+#pragma unroll
+        for (int j = 0; j < PPW; ++j)
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                acc[j][n][0] *= f;
+                acc[j][n][1] *= f;
+            }
+#pragma unroll
+        for (int k = 0; k < PKS; ++k) {
+            const int kt = (pk * PKS + k) * 16;  // first token of the k-step
+            uint32_t ah0 = 0, ah2 = 0, al0 = 0, al2 = 0;
+            if (row) {
+                ah0 = *reinterpret_cast<const uint32_t*>(ph + gid * PROW + kt + 2 * t4);
+                ah2 = *reinterpret_cast<const uint32_t*>(ph + gid * PROW + kt + 8 + 2 * t4);
+                al0 = *reinterpret_cast<const uint32_t*>(pl + gid * PROW + kt + 2 * t4);
+                al2 = *reinterpret_cast<const uint32_t*>(pl + gid * PROW + kt + 8 + 2 * t4);
+            }
+            const int tok = kt + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int j = 0; j < PPW; ++j) {
+                const int chunk = (pw + WN * j) * 2 + (lane >> 4);
+                uint32_t b[4];
+                ldsm_x4_t(base + (KU + chunk * VROW + tok) * 16, b);
+                mma16816(acc[j][0], ah0, ah2, b[0], b[1]);
+                mma16816(acc[j][0], al0, al2, b[0], b[1]);
+                mma16816(acc[j][1], ah0, ah2, b[2], b[3]);
+                mma16816(acc[j][1], al0, al2, b[2], b[3]);
+            }
+        }
+    }
+    cp_wait<0>();
+    __syncthreads();
+
+    // Partial of this split: acc rows gid < G, dims (2 pair + n) 8 + 2 t4.
+    auto rec = [&](int g) { return p.ws + (static_cast<size_t>(h0 + g) * p.splits + split) * (HD + 2); };
+    if constexpr (WK == 1) {
+        if (gid < G)
+#pragma unroll
+            for (int j = 0; j < PPW; ++j)
+#pragma unroll
+                for (int n = 0; n < 2; ++n) {
+                    const int d = ((pw + WN * j) * 2 + n) * 8 + 2 * t4;
+                    *reinterpret_cast<float2*>(rec(gid) + d) = make_float2(acc[j][n][0], acc[j][n][1]);
+                }
+    } else {
+        float* red = reinterpret_cast<float*>(smem);  // [WK][G][HD]
+        if (gid < G)
+#pragma unroll
+            for (int j = 0; j < PPW; ++j)
+#pragma unroll
+                for (int n = 0; n < 2; ++n) {
+                    const int d = ((pw + WN * j) * 2 + n) * 8 + 2 * t4;
+                    *reinterpret_cast<float2*>(red + (pk * G + gid) * HD + d) =
+                        make_float2(acc[j][n][0], acc[j][n][1]);
+                }
+        __syncthreads();
+        for (int i = tid; i < G * HD; i += kAttThreads) {
+            const int g = i / HD, d = i - g * HD;
+            float x = 0.f;
+#pragma unroll
+            for (int k = 0; k < WK; ++k) x += red[(k * G + g) * HD + d];
+            rec(g)[d] = x;
+        }
+    }
+    if (tid < G) {
+        rec(tid)[HD] = s_m[tid];
+        rec(tid)[HD + 1] = s_l[tid];
+    }
+    merge_splits<G>(p, smem, kv);
+}
+
 }  // namespace
 
-// Splits and tokens per CTA for a context length: about two CTAs per SM.
-static void attention_plan(int n_kv, int ctx, int* splits, int* tpc) {
-    int target = (2 * 148 + n_kv - 1) / n_kv;
+// Tokens per sub-tile for a head size: one ring stage holds about 32 KB.
+static int attention_subtile(int hd) {
+    int tt = (8192 / hd) & ~31;
+    return tt < 32 ? 32 : (tt > 256 ? 256 : tt);
+}
+
+// Splits and tokens per CTA: about two CTAs per SM (148 SMs), token ranges a
+// multiple of 16; a CTA's last sub-tile may be partial.
+static void attention_plan(int n_kv, int hd, int ctx, int* splits, int* tpc) {
+    (void)hd;
+    const int target = (2 * 148 + n_kv - 1) / n_kv;
     int t = (ctx + target - 1) / target;
-    t = ((t + 31) / 32) * 32;
-    if (t < 32) t = 32;
+    t = ((t + 15) / 16) * 16;
     *tpc = t;
     *splits = (ctx + t - 1) / t;
 }
 
 size_t attention_workspace_bytes(int n_q, int n_kv, int hd, int ctx) {
     int splits, tpc;
-    attention_plan(n_kv, ctx, &splits, &tpc);
+    attention_plan(n_kv, hd, ctx, &splits, &tpc);
     return 256 + static_cast<size_t>(n_q) * splits * (hd + 2) * sizeof(float) +
            static_cast<size_t>(n_kv) * sizeof(unsigned);
 }
@@ -276,21 +716,24 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     if (n_q <= 0 || n_kv <= 0 || n_q % n_kv != 0)
         return set_error(kErrArg, "n_q=%d must be a positive multiple of n_kv=%d", n_q, n_kv);
     const int G = n_q / n_kv;
-    if (G != 1 && G != 2 && G != 4)
-        return set_error(kErrUnsupported, "query heads per KV head %d (supported: 1, 2, 4)", G);
     if (hd <= 0 || hd % 8 != 0 || hd > 256)
         return set_error(kErrArg, "head_dim=%d must be a multiple of 8 in [8, 256]", hd);
+    const bool tensor = (hd == 64 || hd == 128 || hd == 256) && (G == 1 || G == 2 || G == 4 || G == 8);
+    if (!tensor && G != 1 && G != 2 && G != 4)
+        return set_error(kErrUnsupported,
+                         "query heads per KV head %d (supported: 1, 2, 4; 8 with head_dim 64, 128 or 256)", G);
     if (ctx <= 0) return set_error(kErrArg, "context length %d must be positive", ctx);
     if (ctx_cap < ctx) return set_error(kErrArg, "cache capacity %d below the context length %d", ctx_cap, ctx);
     if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) |
          reinterpret_cast<uintptr_t>(q)) % 16 != 0)
         return set_error(kErrArg, "q and the K/V caches must be 16-byte aligned");
     int splits, tpc;
-    attention_plan(n_kv, ctx, &splits, &tpc);
+    attention_plan(n_kv, hd, ctx, &splits, &tpc);
     const size_t need = attention_workspace_bytes(n_q, n_kv, hd, ctx);
     if (!ws) return set_error(kErrArg, "attention workspace missing");
     if (ws_bytes < need)
         return set_error(kErrArg, "attention workspace holds %zu bytes, needs %zu", ws_bytes, need);
+    if (n_kv * sizeof(unsigned) > 256) return set_error(kErrUnsupported, "more than 64 KV heads");
     AttnParams p = {};
     p.q = q;
     p.q_bits = q_bits;
@@ -306,22 +749,48 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     p.ctx_cap = ctx_cap;
     p.splits = splits;
     p.tpc = tpc;
+    p.tt = attention_subtile(hd);
     p.scale_log2 = scale * kLog2e;
-    if (n_kv * sizeof(unsigned) > 256) return set_error(kErrUnsupported, "more than 64 KV heads");
+    const size_t wts = static_cast<size_t>(G) * splits * sizeof(float);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, n_kv, 1);
     cfg.blockDim = dim3(kAttThreads, 1, 1);
-    cfg.dynamicSmemBytes = static_cast<size_t>(G) * tpc * sizeof(float);
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
     cfg.numAttrs = launch_attrs(attrs, 1);
-    switch (G) {
-        case 1: VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, attention_decode_kernel<1>, p)); break;
-        case 2: VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, attention_decode_kernel<2>, p)); break;
-        default: VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, attention_decode_kernel<4>, p)); break;
+    auto go = [&](auto kern, size_t smem) -> int {
+        if (wts > smem) smem = wts;
+        cfg.dynamicSmemBytes = smem;
+        VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+        return kOk;
+    };
+    if (tensor) {
+        auto pick = [&](auto hd_tag) -> int {
+            constexpr int HD = decltype(hd_tag)::value;
+            const size_t smem = MmaGeo<HD>::smem_bytes;
+            switch (G) {
+                case 1: return go(attention_mma_kernel<1, HD>, smem);
+                case 2: return go(attention_mma_kernel<2, HD>, smem);
+                case 4: return go(attention_mma_kernel<4, HD>, smem);
+                default: return go(attention_mma_kernel<8, HD>, smem);
+            }
+        };
+        if (hd == 64) return pick(std::integral_constant<int, 64>());
+        if (hd == 128) return pick(std::integral_constant<int, 128>());
+        return pick(std::integral_constant<int, 256>());
     }
-    return kOk;
+    const int chunks = hd / 8;
+    size_t smem = static_cast<size_t>(kAttStages) * att_stage_units(p.tt, chunks) * 16 +
+                  static_cast<size_t>(G) * (hd + p.tt) * sizeof(float);
+    const size_t red = static_cast<size_t>(kAttThreads / (hd / 2)) * G * hd * sizeof(float);
+    if (red > smem) smem = red;
+    switch (G) {
+        case 1: return go(attention_decode_kernel<1>, smem);
+        case 2: return go(attention_decode_kernel<2>, smem);
+        default: return go(attention_decode_kernel<4>, smem);
+    }
 }
 
 }  // namespace vkc
