@@ -56,7 +56,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     fn, cap = _noalloc()
-    n_q, n_kv, hd, ctx = 32, 1, 256, 65536  # one KV head: ~300 splits of 32 x 258 floats
+    n_q, n_kv, hd, ctx = 32, 1, 256, 65536  # one KV head: ~300 splits of 32 x 260 floats
     assert lib().vkc_attention_workspace_bytes(n_q, n_kv, hd, ctx) > cap
     rc = fn(None, 16, None, None, None, n_q, n_kv, hd, ctx, 1.0, None)
     assert rc != 0

@@ -17,7 +17,7 @@
 // tokens of one KV head and serves all G query heads of that head, so every K
 // and V byte is read once.  The range streams through a three-stage ring of
 // (K, V) sub-tiles in shared memory filled by 16-byte cp.async copies (zero
-// fill past the end), issued two sub-tiles ahead.  Per sub-tile: lanes split a
+// fill past the end).  Per sub-tile: lanes split a
 // K row into 16-byte chunks and reduce the partial dots; one warp per head
 // updates the running maximum and sum (base-2 online softmax) and rescales;
 // threads own one output dimension for all G heads and a share of the tokens
@@ -32,10 +32,39 @@
 #include <type_traits>
 
 namespace vkc {
-namespace {
 
 constexpr int kAttThreads = 256;
 constexpr int kAttStages = 3;
+
+// Ring geometry of the tensor-core decode attention kernels for one head_dim.
+template <int HD>
+struct MmaGeo {
+    static constexpr int CH = HD / 8;              // 16-byte chunks per K row
+    static constexpr int TT = 8192 / HD;           // tokens per sub-tile (32 KB of K + V)
+    static constexpr int KROW = CH + 1;            // K row pitch (units), padded
+    static constexpr int VROW = TT + 1;            // V run pitch (units), padded
+    static constexpr int KU = TT * KROW;
+    static constexpr int SU = KU + CH * VROW;      // units per ring stage
+    static constexpr int NT = TT / 8;              // token tiles (scores n-tiles)
+    static constexpr int KG = NT >= 8 ? 1 : 8 / NT;          // warps sharing a token tile
+    static constexpr int TPW = NT >= 8 ? NT / 8 : 1;         // token tiles per warp
+    static constexpr int KS = HD / 16 / KG;                  // score k-steps per warp
+    static constexpr int NP = HD / 16;             // pairs of 8-dimension n-tiles
+    static constexpr int WN = NP < 8 ? NP : 8;     // warps along dimensions
+    static constexpr int WK = 8 / WN;              // warps along tokens
+    static constexpr int PPW = NP / WN;            // dimension pairs per warp
+    static constexpr int PKS = TT / 16 / WK;       // P.V k-steps per warp
+    static constexpr int PROW = TT + 8;            // halves per P row (conflict-free A loads)
+    static constexpr size_t ring_bytes = static_cast<size_t>(kAttStages) * SU * 16;
+    static constexpr size_t sc_bytes = static_cast<size_t>(KG) * 8 * TT * sizeof(float);
+    static constexpr size_t p_bytes = 2ull * 8 * PROW * sizeof(__half);
+    static constexpr size_t q_bytes = static_cast<size_t>(HD / 16) * 32 * 16;
+    static constexpr size_t smem_bytes = ring_bytes + sc_bytes + p_bytes + q_bytes;
+    static_assert(KS % 2 == 0 && NT * KG >= 8 && WN * WK == 8 && PKS >= 1, "geometry");
+};
+
+namespace {
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnParams {
@@ -44,12 +73,14 @@ struct AttnParams {
     const uint4* kc;
     const uint4* vc;
     float* out;
-    float* ws;          // [n_q][splits][hd + 2] : acc[hd], m, l
+    float* ws;          // [n_q][splits][pitch] : acc[hd], m, l (pitch = hd + 4)
     unsigned* tickets;  // [n_kv]
     int n_q, n_kv, hd, ctx, splits, tpc;
     int ctx_cap;        // V run length per (head, chunk): the cache capacity
     int tt;             // tokens per sub-tile (a multiple of 32)
     float scale_log2;   // scale * log2(e)
+    int pitch;          // floats per partial record, hd + 4 (a multiple of 4)
+    int smem;           // dynamic shared memory of the launch (bytes)
 };
 
 // One ring stage in 16-byte units: K sub-tile [tt][chunks], then the V
@@ -103,60 +134,142 @@ __device__ __forceinline__ float reduce_heads(float (&v)[G], int lane, int lpt, 
     return r;
 }
 
-// The last CTA of KV head `kv` to finish (atomic ticket) merges the splits of
-// its G query heads in split order and resets the ticket for the next launch.
-// Split weights w[g][s] = 2^(m_s - max) / sum_s 2^(m_s - max) l_s go to `smem`
-// (free by now); out = sum_s w[g][s] acc_s.
-template <int G>
-__device__ __forceinline__ void merge_splits(const AttnParams& p, uint8_t* smem, int kv) {
+// The last CTA of KV head `kv` to finish (atomic ticket) merges the S partial
+// records of its G query heads in order and resets the ticket for the next
+// launch:
+//   w[g][s] = 2^(m_s - max_s m_s) / sum_s 2^(m_s - max_s m_s) l_s
+//   out[g]  = sum_s w[g][s] acc_s
+// The merge is on the critical path of every launch and is a chain of L2
+// round trips, so it is kept short: when the G heads' records (contiguous in
+// the workspace) fit in the CTA's shared memory they are staged with one
+// round of 16-byte cp.async copies and merged there; otherwise they are read
+// with many loads in flight per thread.
+template <int G, int NT = kAttThreads>
+__device__ __forceinline__ void merge_splits(const AttnParams& p, uint8_t* smem, int kv, int S) {
     __shared__ unsigned s_ticket;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hd = p.hd, h0 = kv * G;
-    __threadfence();
+    const int hd = p.hd, h0 = kv * G, pitch = p.pitch;
+    __threadfence();  // this thread's partial writes, before the ticket
     __syncthreads();
     if (tid == 0) s_ticket = atomicAdd(p.tickets + kv, 1u);
     __syncthreads();
-    if (s_ticket != static_cast<unsigned>(p.splits - 1)) return;
+    if (s_ticket != static_cast<unsigned>(S - 1)) return;
     __threadfence();
-    float* wts = reinterpret_cast<float*>(smem);  // [G][splits]
-    for (int i = tid; i < G * p.splits; i += kAttThreads) {
-        const int g = i / p.splits, s2 = i - g * p.splits;
-        wts[i] = __ldcg(p.ws + (static_cast<size_t>(h0 + g) * p.splits + s2) * (hd + 2) + hd);
-    }
-    __syncthreads();
-    if (warp < G) {
-        const int g = warp;
-        const float* rb = p.ws + static_cast<size_t>(h0 + g) * p.splits * (hd + 2) + hd;
-        float m = -INFINITY;
-        for (int s2 = lane; s2 < p.splits; s2 += 32) m = fmaxf(m, wts[g * p.splits + s2]);
+    const float* src = p.ws + static_cast<size_t>(h0) * S * pitch;  // [G][S][pitch]
+    const size_t rec_bytes = static_cast<size_t>(G) * S * pitch * sizeof(float);
+    float* wts = reinterpret_cast<float*>(smem + rec_bytes);        // [G][S]
+    if (rec_bytes + static_cast<size_t>(G) * S * sizeof(float) <= static_cast<size_t>(p.smem)) {
+        const float* st = reinterpret_cast<const float*>(smem);
+        const uint32_t dst = smem_addr(smem);
+        const int units = static_cast<int>(rec_bytes / 16);
+        for (int u = tid; u < units; u += NT) cp_async16_zfill(dst + u * 16, src + 4 * u, true);
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        for (int g = warp; g < G; g += NT / 32) {
+            float m = -INFINITY;
+            for (int s2 = lane; s2 < S; s2 += 32) m = fmaxf(m, st[(g * S + s2) * pitch + hd]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float den = 0.f;
-        for (int s2 = lane; s2 < p.splits; s2 += 32) {
-            const float w = exp2f(wts[g * p.splits + s2] - m);
-            wts[g * p.splits + s2] = w;
-            den = fmaf(w, __ldcg(rb + s2 * (hd + 2) + 1), den);
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float den = 0.f;
+            for (int s2 = lane; s2 < S; s2 += 32) {
+                const float* r = st + (g * S + s2) * pitch + hd;
+                const float w = exp2f(r[0] - m);
+                wts[g * S + s2] = w;
+                den = fmaf(w, r[1], den);
+            }
+            den = warp_sum(den);
+            const float inv = 1.f / den;
+            __syncwarp();
+            for (int s2 = lane; s2 < S; s2 += 32) wts[g * S + s2] *= inv;
         }
-        den = warp_sum(den);
-        const float inv = 1.f / den;
-        __syncwarp();
-        for (int s2 = lane; s2 < p.splits; s2 += 32) wts[g * p.splits + s2] *= inv;
-    }
-    __syncthreads();
-    for (int i = tid; i < G * hd; i += kAttThreads) {
-        const int g = i / hd, d = i - g * hd;
-        const float* rb = p.ws + static_cast<size_t>(h0 + g) * p.splits * (hd + 2) + d;
-        const float* w = wts + g * p.splits;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        int s2 = 0;
-        for (; s2 + 4 <= p.splits; s2 += 4) {
-            a0 = fmaf(w[s2], __ldcg(rb + (s2) * (hd + 2)), a0);
-            a1 = fmaf(w[s2 + 1], __ldcg(rb + (s2 + 1) * (hd + 2)), a1);
-            a2 = fmaf(w[s2 + 2], __ldcg(rb + (s2 + 2) * (hd + 2)), a2);
-            a3 = fmaf(w[s2 + 3], __ldcg(rb + (s2 + 3) * (hd + 2)), a3);
+        __syncthreads();
+        for (int i = tid; i < G * hd; i += NT) {
+            const int g = i / hd, d = i - g * hd;
+            const float* r = st + g * S * pitch + d;
+            const float* w = wts + g * S;
+            float a0 = 0.f, a1 = 0.f;
+            int s2 = 0;
+            for (; s2 + 1 < S; s2 += 2) {
+                a0 = fmaf(w[s2], r[s2 * pitch], a0);
+                a1 = fmaf(w[s2 + 1], r[(s2 + 1) * pitch], a1);
+            }
+            if (s2 < S) a0 = fmaf(w[s2], r[s2 * pitch], a0);
+            p.out[static_cast<size_t>(h0) * hd + i] = a0 + a1;
         }
-        for (; s2 < p.splits; ++s2) a0 = fmaf(w[s2], __ldcg(rb + s2 * (hd + 2)), a0);
-        p.out[static_cast<size_t>(h0 + g) * hd + d] = (a0 + a1) + (a2 + a3);
+    } else {
+        // (m, l) of every (head, split), then four dimensions per thread with
+        // the splits divided among thread groups, combined in fixed order.
+        float2* ml = reinterpret_cast<float2*>(smem);                // [G][S]
+        float* w2 = reinterpret_cast<float*>(ml + G * S);            // [G][S]
+        for (int i = tid; i < G * S; i += NT)
+            ml[i] = __ldcg(reinterpret_cast<const float2*>(src + static_cast<size_t>(i) * pitch + hd));
+        __syncthreads();
+        for (int g = warp; g < G; g += NT / 32) {
+            float m = -INFINITY;
+            for (int s2 = lane; s2 < S; s2 += 32) m = fmaxf(m, ml[g * S + s2].x);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float den = 0.f;
+            for (int s2 = lane; s2 < S; s2 += 32) {
+                const float2 v = ml[g * S + s2];
+                const float w = exp2f(v.x - m);
+                w2[g * S + s2] = w;
+                den = fmaf(w, v.y, den);
+            }
+            den = warp_sum(den);
+            const float inv = 1.f / den;
+            __syncwarp();
+            for (int s2 = lane; s2 < S; s2 += 32) w2[g * S + s2] *= inv;
+        }
+        __syncthreads();
+        const int quads = G * hd / 4;
+        const int ngroups = quads >= NT ? 1 : NT / quads;
+        float4* part = reinterpret_cast<float4*>(smem + ((static_cast<size_t>(G) * S * 12 + 15) & ~size_t(15)));
+        for (int qd = tid % quads; qd < quads; qd += NT) {
+            const int grp = tid / quads;
+            if (grp >= ngroups) break;
+            const int g = (qd * 4) / hd, d = qd * 4 - g * hd;
+            const float* rb = src + static_cast<size_t>(g) * S * pitch + d;
+            const float* w = w2 + g * S;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            int s2 = grp;
+            for (; s2 + 7 * ngroups < S; s2 += 8 * ngroups) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    v[u] = __ldcg(reinterpret_cast<const float4*>(rb + static_cast<size_t>(s2 + u * ngroups) * pitch));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float wu = w[s2 + u * ngroups];
+                    acc.x = fmaf(wu, v[u].x, acc.x);
+                    acc.y = fmaf(wu, v[u].y, acc.y);
+                    acc.z = fmaf(wu, v[u].z, acc.z);
+                    acc.w = fmaf(wu, v[u].w, acc.w);
+                }
+            }
+            for (; s2 < S; s2 += ngroups) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(rb + static_cast<size_t>(s2) * pitch));
+                const float wu = w[s2];
+                acc.x = fmaf(wu, v.x, acc.x);
+                acc.y = fmaf(wu, v.y, acc.y);
+                acc.z = fmaf(wu, v.z, acc.z);
+                acc.w = fmaf(wu, v.w, acc.w);
+            }
+            part[grp * quads + qd] = acc;
+        }
+        __syncthreads();
+        for (int qd = tid; qd < quads; qd += NT) {
+            float4 acc = part[qd];
+            for (int grp = 1; grp < ngroups; ++grp) {
+                const float4 v = part[grp * quads + qd];
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            *reinterpret_cast<float4*>(p.out + static_cast<size_t>(h0) * hd + qd * 4) = acc;
+        }
     }
     if (tid == 0) p.tickets[kv] = 0u;
 }
@@ -362,15 +475,15 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_decode_kernel(const 
         const int g = i / hd, d = i - g * hd;
         float v = 0.f;
         for (int q = 0; q < ntg; ++q) v += red[(q * G + g) * hd + d];
-        p.ws[(static_cast<size_t>(h0 + g) * p.splits + split) * (hd + 2) + d] = v;
+        p.ws[(static_cast<size_t>(h0 + g) * p.splits + split) * p.pitch + d] = v;
     }
     if (tid < G) {
-        float* rec = p.ws + (static_cast<size_t>(h0 + tid) * p.splits + split) * (hd + 2) + hd;
+        float* rec = p.ws + (static_cast<size_t>(h0 + tid) * p.splits + split) * p.pitch + hd;
         rec[0] = s_m[tid];
         rec[1] = s_l[tid];
     }
 
-    merge_splits<G>(p, smem, kv);
+    merge_splits<G>(p, smem, kv, p.splits);
 }
 
 // ---- tensor-core variant (head_dim 64 / 128 / 256) ---------------------------
@@ -414,31 +527,6 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
     lo = h2_bits(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
 }
 
-template <int HD>
-struct MmaGeo {
-    static constexpr int CH = HD / 8;              // 16-byte chunks per K row
-    static constexpr int TT = 8192 / HD;           // tokens per sub-tile (32 KB of K + V)
-    static constexpr int KROW = CH + 1;            // K row pitch (units), padded
-    static constexpr int VROW = TT + 1;            // V run pitch (units), padded
-    static constexpr int KU = TT * KROW;
-    static constexpr int SU = KU + CH * VROW;      // units per ring stage
-    static constexpr int NT = TT / 8;              // token tiles (scores n-tiles)
-    static constexpr int KG = NT >= 8 ? 1 : 8 / NT;          // warps sharing a token tile
-    static constexpr int TPW = NT >= 8 ? NT / 8 : 1;         // token tiles per warp
-    static constexpr int KS = HD / 16 / KG;                  // score k-steps per warp
-    static constexpr int NP = HD / 16;             // pairs of 8-dimension n-tiles
-    static constexpr int WN = NP < 8 ? NP : 8;     // warps along dimensions
-    static constexpr int WK = 8 / WN;              // warps along tokens
-    static constexpr int PPW = NP / WN;            // dimension pairs per warp
-    static constexpr int PKS = TT / 16 / WK;       // P.V k-steps per warp
-    static constexpr int PROW = TT + 8;            // halves per P row (conflict-free A loads)
-    static constexpr size_t ring_bytes = static_cast<size_t>(kAttStages) * SU * 16;
-    static constexpr size_t sc_bytes = static_cast<size_t>(KG) * 8 * TT * sizeof(float);
-    static constexpr size_t p_bytes = 2ull * 8 * PROW * sizeof(__half);
-    static constexpr size_t q_bytes = static_cast<size_t>(HD / 16) * 32 * 16;
-    static constexpr size_t smem_bytes = ring_bytes + sc_bytes + p_bytes + q_bytes;
-    static_assert(KS % 2 == 0 && NT * KG >= 8 && WN * WK == 8 && PKS >= 1, "geometry");
-};
 
 template <int G, int HD>
 __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const AttnParams p) {
@@ -494,8 +582,10 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
             cp_async16_zfill(base + (v_dst0 + i * (256 / TT) * VROW) * 16, src, vok);
         }
     };
+    // All ring slots are filled up front; a slot is refilled once its
+    // sub-tile has been consumed, so three sub-tiles are in flight.
 #pragma unroll
-    for (int s = 0; s < kAttStages - 1; ++s) {
+    for (int s = 0; s < kAttStages; ++s) {
         if (s < nsub) issue(s);
         cp_commit();
     }
@@ -539,10 +629,8 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
     const int pw = warp % WN, pk = warp / WN;  // P.V: dimension pairs pw + WN j, k-steps of group pk
 
     for (int s = 0; s < nsub; ++s) {
-        cp_wait<kAttStages - 2>();
-        __syncthreads();  // sub-tile s landed for all; sub-tile s-1 fully consumed
-        if (s + kAttStages - 1 < nsub) issue(s + kAttStages - 1);
-        cp_commit();
+        cp_wait<kAttStages - 1>();
+        __syncthreads();  // sub-tile s landed for all threads
         const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
         const int nt = min(TT, T - s * TT);
 
@@ -550,7 +638,8 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
 #pragma unroll
         for (int j = 0; j < TPW; ++j) {
             const int tile = KG == 1 ? warp + 8 * j : warp % NT;
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            // Two accumulators (even / odd k-steps) halve the dependent MMA chain.
+            float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
             const int tok = tile * 8 + (lane & 7);
 #pragma unroll
             for (int ks = 0; ks < KS; ks += 2) {
@@ -559,14 +648,15 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
                 ldsm_x4(base + (tok * KROW + chunk) * 16, b);
                 const uint4 qa = qf[(kgi * KS + ks) * 32 + lane], qb = qf[(kgi * KS + ks + 1) * 32 + lane];
                 mma16816(c, qa.x, qa.y, b[0], b[1]);
-                mma16816(c, qb.x, qb.y, b[2], b[3]);
+                mma16816(c2, qb.x, qb.y, b[2], b[3]);
                 if (q_lo) {
                     mma16816(c, qa.z, qa.w, b[0], b[1]);
-                    mma16816(c, qb.z, qb.w, b[2], b[3]);
+                    mma16816(c2, qb.z, qb.w, b[2], b[3]);
                 }
             }
             if (gid < G)
-                *reinterpret_cast<float2*>(sc + (kgi * 8 + gid) * TT + tile * 8 + 2 * t4) = make_float2(c[0], c[1]);
+                *reinterpret_cast<float2*>(sc + (kgi * 8 + gid) * TT + tile * 8 + 2 * t4) =
+                    make_float2(c[0] + c2[0], c[1] + c2[1]);
         }
         __syncthreads();
 
@@ -640,12 +730,15 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
                 mma16816(acc[j][1], al0, al2, b[2], b[3]);
             }
         }
+        __syncthreads();  // slot of sub-tile s consumed by all warps
+        if (s + kAttStages < nsub) issue(s + kAttStages);
+        cp_commit();
     }
     cp_wait<0>();
     __syncthreads();
 
     // Partial of this split: acc rows gid < G, dims (2 pair + n) 8 + 2 t4.
-    auto rec = [&](int g) { return p.ws + (static_cast<size_t>(h0 + g) * p.splits + split) * (HD + 2); };
+    auto rec = [&](int g) { return p.ws + (static_cast<size_t>(h0 + g) * p.splits + split) * p.pitch; };
     if constexpr (WK == 1) {
         if (gid < G)
 #pragma unroll
@@ -679,7 +772,346 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
         rec(tid)[HD] = s_m[tid];
         rec(tid)[HD + 1] = s_l[tid];
     }
-    merge_splits<G>(p, smem, kv);
+    merge_splits<G>(p, smem, kv, p.splits);
+}
+
+// ---- token-slice variant with swapped operands (head_dim 64 / 128) ----------
+//
+// Four warps per CTA; each owns 16-token slices of every sub-tile and runs the
+// whole step on them with the tokens, not the (few) query heads, as the M
+// dimension of mma.sync m16n8k16, so no MMA rows are padding:
+//   scores  S^T[16 tok][8 heads] = K[16 tok][hd] . q^T[hd][8 heads]     A = K  (ldmatrix)
+//   P.V     O^T[hd][8 heads]    += V^T[hd][16 tok] . P^T[16 tok][8 heads] A = V^T (ldmatrix.trans)
+// Heads G..7 of the 8 columns carry zero q and zero p.  Each warp keeps its own
+// online softmax (running max and sum per head, in registers); P^T goes from
+// the score accumulators to the B operand of P.V through movmatrix (a
+// register transpose), so p never touches shared memory and the warps meet
+// only at the two ring barriers per sub-tile.  q and p are fp32 values split
+// into fp16 high and low parts, both multiplied (about 22 significant bits).
+// The four warp states are merged through shared memory at the end.
+constexpr int kFaThreads = 128;
+constexpr int kFaCluster = 8;  // CTAs per cluster (consecutive splits of one KV head)
+
+__device__ __forceinline__ void mma16816_full(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+template <int G, int HD>
+__global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnParams p) {
+    using Geo = MmaGeo<HD>;
+    constexpr int CH = Geo::CH, TT = Geo::TT, KROW = Geo::KROW, VROW = Geo::VROW, KU = Geo::KU, SU = Geo::SU;
+    constexpr int NW = kFaThreads / 32;    // warps
+    constexpr int SPW = TT / (16 * NW);    // 16-token slices per warp per sub-tile
+    constexpr int KS = HD / 16;            // score k-steps
+    constexpr int MT = HD / 16;            // P.V m-tiles of 16 dimensions
+    constexpr int CPT = 1024 / kFaThreads; // K (and V) copies per thread per sub-tile
+    static_assert(SPW >= 1 && TT % (16 * NW) == 0 && KS % 2 == 0, "geometry");
+    static_assert(kFaThreads % CH == 0 && kFaThreads % TT == 0, "copy plan");
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_wm[NW][8], s_wl[NW][8];
+
+    const int split = blockIdx.x, kv = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gid = lane >> 2, t4 = lane & 3;
+    const int t0 = split * p.tpc;
+    const int T = min(p.tpc, p.ctx - t0);
+    const int nsub = (T + TT - 1) / TT;
+    const int h0 = kv * G;
+    uint4* ring = reinterpret_cast<uint4*>(smem);
+    uint4* qf = reinterpret_cast<uint4*>(smem + Geo::ring_bytes);  // [KS][32]
+
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // Copy plan: K chunk tid % CH of tokens tid / CH + i (128 / CH); V token
+    // tid % TT of chunks tid / TT + i (128 / TT); i < CPT.
+    const int k_tok = tid / CH, k_chk = tid % CH;
+    const int v_tok = tid % TT, v_chk = tid / TT;
+    const uint4* k_src0 = p.kc + (static_cast<size_t>(t0 + k_tok) * p.n_kv + kv) * CH + k_chk;
+    const size_t k_step = static_cast<size_t>(kFaThreads / CH) * p.n_kv * CH;
+    const uint4* v_src0 = p.vc + (static_cast<size_t>(kv) * CH + v_chk) * p.ctx_cap + t0 + v_tok;
+    const size_t v_step = static_cast<size_t>(kFaThreads / TT) * p.ctx_cap;
+    const int k_dst0 = k_tok * KROW + k_chk, v_dst0 = KU + v_chk * VROW + v_tok;
+    auto issue = [&](int s) {
+        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const int nt = min(TT, T - s * TT);
+        const size_t tok = static_cast<size_t>(s) * TT;
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int t = k_tok + i * (kFaThreads / CH);
+            const bool ok = t < nt;
+            const uint4* src = ok ? k_src0 + tok * p.n_kv * CH + i * k_step : p.kc;
+            cp_async16_zfill(base + (k_dst0 + i * (kFaThreads / CH) * KROW) * 16, src, ok);
+        }
+        const bool vok = v_tok < nt;
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const uint4* src = vok ? v_src0 + tok + i * v_step : p.vc;
+            cp_async16_zfill(base + (v_dst0 + i * (kFaThreads / TT) * VROW) * 16, src, vok);
+        }
+    };
+#pragma unroll
+    for (int s = 0; s < kAttStages; ++s) {
+        if (s < nsub) issue(s);
+        cp_commit();
+    }
+
+    // q^T as B fragments in shared memory: entry (k-step, lane) =
+    // {hi b0, hi b1, lo b0, lo b1}, b0 = q[gid][16 k + 2 t4 ..], b1 = +8.
+    for (int e = tid; e < KS * 32; e += kFaThreads) {
+        const int kj = e >> 5, g = (e & 31) >> 2, q4 = e & 3;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (g < G) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const size_t qi = static_cast<size_t>(h0 + g) * HD + kj * 16 + half * 8 + 2 * q4;
+                float2 f;
+                if (p.q_bits == 16)
+                    f = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(p.q) + qi));
+                else
+                    f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(p.q) + qi);
+                x[2 * half] = f.x;
+                x[2 * half + 1] = f.y;
+            }
+        }
+        uint4 fr;
+        split_pair(x[0], x[1], fr.x, fr.z);
+        split_pair(x[2], x[3], fr.y, fr.w);
+        qf[e] = fr;
+    }
+    const bool q_lo = p.q_bits != 16;  // fp16 q has no low part
+    // This lane's two heads (columns 2 t4, 2 t4 + 1) and whether they exist.
+    const bool hv0 = 2 * t4 < G, hv1 = 2 * t4 + 1 < G;
+
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // l: this lane's share
+    float acc[MT][4];  // O^T: (dim 16 mt + gid [+8], head 2 t4 [+1])
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+
+    for (int s = 0; s < nsub; ++s) {
+        cp_wait<kAttStages - 1>();
+        __syncthreads();  // sub-tile s landed for all threads (and q fragments, first time)
+        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const int nt = min(TT, T - s * TT);
+#pragma unroll
+        for (int sl = 0; sl < SPW; ++sl) {
+            const int ts0 = (warp * SPW + sl) * 16;  // first token of the slice
+
+            // scores S^T; two accumulators (even / odd k-steps) halve the MMA chain
+            float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+            const int tok = ts0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int kj = 0; kj < KS; ++kj) {
+                uint32_t a[4];
+                ldsm_x4(base + (tok * KROW + 2 * kj + (lane >> 4)) * 16, a);
+                const uint4 qb = qf[kj * 32 + lane];
+                if (kj & 1) {
+                    mma16816_full(c2, a, qb.x, qb.y);
+                    if (q_lo) mma16816_full(c2, a, qb.z, qb.w);
+                } else {
+                    mma16816_full(c, a, qb.x, qb.y);
+                    if (q_lo) mma16816_full(c, a, qb.z, qb.w);
+                }
+            }
+            // sv[i]: i = 0 (token gid, head 2t4), 1 (gid, 2t4+1), 2 (gid+8, 2t4), 3 (gid+8, 2t4+1)
+            float sv[4];
+            const bool tv0 = ts0 + gid < nt, tv1 = ts0 + gid + 8 < nt;
+            sv[0] = tv0 && hv0 ? (c[0] + c2[0]) * p.scale_log2 : -INFINITY;
+            sv[1] = tv0 && hv1 ? (c[1] + c2[1]) * p.scale_log2 : -INFINITY;
+            sv[2] = tv1 && hv0 ? (c[2] + c2[2]) * p.scale_log2 : -INFINITY;
+            sv[3] = tv1 && hv1 ? (c[3] + c2[3]) * p.scale_log2 : -INFINITY;
+            // online softmax per head: a head's 16 tokens sit in the 8 lanes of one t4
+            float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+            }
+            const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+            const float f0 = mn0 == -INFINITY ? 1.f : exp2f(m_run[0] - mn0);
+            const float f1 = mn1 == -INFINITY ? 1.f : exp2f(m_run[1] - mn1);
+            float pv[4];
+            pv[0] = sv[0] == -INFINITY ? 0.f : exp2f(sv[0] - mn0);
+            pv[1] = sv[1] == -INFINITY ? 0.f : exp2f(sv[1] - mn1);
+            pv[2] = sv[2] == -INFINITY ? 0.f : exp2f(sv[2] - mn0);
+            pv[3] = sv[3] == -INFINITY ? 0.f : exp2f(sv[3] - mn1);
+            l_run[0] = fmaf(l_run[0], f0, pv[0] + pv[2]);
+            l_run[1] = fmaf(l_run[1], f1, pv[1] + pv[3]);
+            m_run[0] = mn0;
+            m_run[1] = mn1;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                acc[mt][0] *= f0;
+                acc[mt][1] *= f1;
+                acc[mt][2] *= f0;
+                acc[mt][3] *= f1;
+            }
+            // P^T as B fragments (k = tokens, n = heads): transpose the 8x8
+            // blocks [token][head] of the accumulator layout in registers.
+            uint32_t x0h, x0l, x1h, x1l;
+            split_pair(pv[0], pv[1], x0h, x0l);  // tokens 0..7 of the slice
+            split_pair(pv[2], pv[3], x1h, x1l);  // tokens 8..15
+            const uint32_t bh0 = movmatrix_t(x0h), bh1 = movmatrix_t(x1h);
+            const uint32_t bl0 = movmatrix_t(x0l), bl1 = movmatrix_t(x1l);
+
+            // P.V: A = V^T m-tile (chunks 2 mt, 2 mt + 1) x the slice's 16 tokens
+            const int tokv = ts0 + (lane & 7) + ((lane >> 4) & 1) * 8;
+            const int chv = (lane >> 3) & 1;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                uint32_t a[4];
+                ldsm_x4_t(base + (KU + (2 * mt + chv) * VROW + tokv) * 16, a);
+                mma16816_full(acc[mt], a, bh0, bh1);
+                mma16816_full(acc[mt], a, bl0, bl1);
+            }
+        }
+        __syncthreads();  // slot of sub-tile s consumed by all warps
+        if (s + kAttStages < nsub) issue(s + kAttStages);
+        cp_commit();
+    }
+    cp_wait<0>();
+
+    // Merge the warp states of this CTA (the ring is free now).
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
+        l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
+    }
+    if (gid == 0) {
+        s_wm[warp][2 * t4] = m_run[0];
+        s_wm[warp][2 * t4 + 1] = m_run[1];
+        s_wl[warp][2 * t4] = l_run[0];
+        s_wl[warp][2 * t4 + 1] = l_run[1];
+    }
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);  // [NW][G][HD]
+    {
+        float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            M0 = fmaxf(M0, s_wm[w][2 * t4]);
+            M1 = fmaxf(M1, s_wm[w][2 * t4 + 1]);
+        }
+        const float sw0 = m_run[0] == -INFINITY ? 0.f : exp2f(m_run[0] - M0);
+        const float sw1 = m_run[1] == -INFINITY ? 0.f : exp2f(m_run[1] - M1);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const int d = 16 * mt + gid;
+            if (hv0) {
+                red[(warp * G + 2 * t4) * HD + d] = acc[mt][0] * sw0;
+                red[(warp * G + 2 * t4) * HD + d + 8] = acc[mt][2] * sw0;
+            }
+            if (hv1) {
+                red[(warp * G + 2 * t4 + 1) * HD + d] = acc[mt][1] * sw1;
+                red[(warp * G + 2 * t4 + 1) * HD + d + 8] = acc[mt][3] * sw1;
+            }
+        }
+    }
+    __syncthreads();
+    // This CTA's record in shared memory, [G][HD + 4]: acc[HD], m, l.
+    constexpr int RP = HD + 4;
+    float* crec = red + NW * G * HD;
+    for (int i = tid; i < G * HD; i += kFaThreads) {
+        const int g = i / HD, d = i - g * HD;
+        float x = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) x += red[(w * G + g) * HD + d];
+        crec[g * RP + d] = x;
+    }
+    if (tid < G) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, s_wm[w][tid]);
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float mw = s_wm[w][tid];
+            L += mw == -INFINITY ? 0.f : s_wl[w][tid] * exp2f(mw - M);
+        }
+        crec[tid * RP + HD] = M;
+        crec[tid * RP + HD + 1] = L;
+    }
+
+    // ---- cluster of kFaCluster consecutive splits: rank 0 merges the records
+    // of its peers through distributed shared memory.  Barrier 1 publishes the
+    // records; barrier 2 keeps the peers resident until rank 0 has read them.
+    __syncthreads();
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    if (rank != 0) {
+        cluster_arrive_release();
+        cluster_wait_acquire();
+        return;
+    }
+    __shared__ float s_cM[8], s_cL[8];
+    const uint32_t crec_addr = smem_addr(crec);
+    // Four dimensions per thread: the (m, l) and values of every rank are
+    // loaded in one round, then summed in rank order.
+    const int nc = p.splits / kFaCluster, cidx = split / kFaCluster;
+    for (int qd = tid; qd < G * HD / 4; qd += kFaThreads) {
+        const int g = (qd * 4) / HD, d = qd * 4 - g * HD;
+        float4 v[kFaCluster];
+        float2 ml[kFaCluster];
+#pragma unroll
+        for (int r = 0; r < kFaCluster; ++r) {
+            const uint32_t ra = map_cluster_addr(crec_addr + (g * RP + d) * 4, r);
+            const uint32_t rs = map_cluster_addr(crec_addr + (g * RP + HD) * 4, r);
+            asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(v[r].x), "=f"(v[r].y), "=f"(v[r].z), "=f"(v[r].w)
+                         : "r"(ra)
+                         : "memory");
+            asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(ml[r].x), "=f"(ml[r].y) : "r"(rs) : "memory");
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kFaCluster; ++r) M = fmaxf(M, ml[r].x);
+        float L = 0.f;
+        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < kFaCluster; ++r) {
+            const float w = ml[r].x == -INFINITY ? 0.f : exp2f(ml[r].x - M);
+            L = fmaf(w, ml[r].y, L);
+            acc4.x = fmaf(w, v[r].x, acc4.x);
+            acc4.y = fmaf(w, v[r].y, acc4.y);
+            acc4.z = fmaf(w, v[r].z, acc4.z);
+            acc4.w = fmaf(w, v[r].w, acc4.w);
+        }
+        if (nc == 1) {
+            const float inv = 1.f / L;
+            *reinterpret_cast<float4*>(p.out + static_cast<size_t>(h0) * HD + qd * 4) =
+                make_float4(acc4.x * inv, acc4.y * inv, acc4.z * inv, acc4.w * inv);
+        } else {
+            *reinterpret_cast<float4*>(p.ws + (static_cast<size_t>(h0 + g) * nc + cidx) * p.pitch + d) = acc4;
+            if (d == 0) {
+                s_cM[g] = M;
+                s_cL[g] = L;
+            }
+        }
+    }
+    cluster_arrive_release();  // peers' records have been read
+    if (nc > 1) {
+        __syncthreads();
+        if (tid < G) {
+            float* r = p.ws + (static_cast<size_t>(h0 + tid) * nc + cidx) * p.pitch + HD;
+            r[0] = s_cM[tid];
+            r[1] = s_cL[tid];
+        }
+        merge_splits<G, kFaThreads>(p, smem, kv, nc);
+    }
+    cluster_wait_acquire();
 }
 
 }  // namespace
@@ -690,21 +1122,58 @@ static int attention_subtile(int hd) {
     return tt < 32 ? 32 : (tt > 256 ? 256 : tt);
 }
 
-// Splits and tokens per CTA: about two CTAs per SM (148 SMs), token ranges a
-// multiple of 16; a CTA's last sub-tile may be partial.
-static void attention_plan(int n_kv, int hd, int ctx, int* splits, int* tpc) {
-    (void)hd;
-    const int target = (2 * 148 + n_kv - 1) / n_kv;
+// Which kernel serves a shape, and how the context is split.
+struct AttnPlan {
+    enum Kind { kSimt, kMma, kSlice } kind;
+    int splits;   // CTAs per KV head (grid x)
+    int tpc;      // tokens per CTA (a multiple of 16)
+    int records;  // partial records per query head in the workspace
+};
+
+// Splits: about two CTAs per SM (148 SMs), but at least three sub-tiles
+// (~96 KB of cache) per CTA, so a small cache (a shard with one KV head) is
+// not cut into many tiny splits whose merge would dominate.  The token-slice
+// kernel groups its splits in clusters of kFaCluster and keeps one record per
+// cluster; at most 32 clusters (256 CTAs) are launched, which two CTAs per SM
+// hold at once.  A CTA's last sub-tile may be partial, and with clusters the
+// last CTAs of a head may get no tokens at all.
+static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
+    AttnPlan pl;
+    const int G = n_q / n_kv;
+    const bool mma_g = G == 1 || G == 2 || G == 4 || G == 8;
+    pl.kind = (hd == 64 || hd == 128) && mma_g ? AttnPlan::kSlice
+              : (hd == 256 && mma_g)           ? AttnPlan::kMma
+                                               : AttnPlan::kSimt;
+    const int min_tpc = 3 * (8192 / hd);
+    const int by_size = (ctx + min_tpc - 1) / min_tpc;
+    int target;
+    if (pl.kind == AttnPlan::kSlice) {
+        int nc = 32 / n_kv;
+        const int nc_size = (by_size + kFaCluster - 1) / kFaCluster;
+        if (nc_size < nc) nc = nc_size;
+        if (nc < 1) nc = 1;
+        target = nc * kFaCluster;
+    } else {
+        target = (2 * 148 + n_kv - 1) / n_kv;
+        if (by_size < target) target = by_size;
+        if (target < 1) target = 1;
+    }
     int t = (ctx + target - 1) / target;
     t = ((t + 15) / 16) * 16;
-    *tpc = t;
-    *splits = (ctx + t - 1) / t;
+    pl.tpc = t;
+    if (pl.kind == AttnPlan::kSlice) {
+        pl.splits = target;
+        pl.records = target / kFaCluster;
+    } else {
+        pl.splits = (ctx + t - 1) / t;
+        pl.records = pl.splits;
+    }
+    return pl;
 }
 
 size_t attention_workspace_bytes(int n_q, int n_kv, int hd, int ctx) {
-    int splits, tpc;
-    attention_plan(n_kv, hd, ctx, &splits, &tpc);
-    return 256 + static_cast<size_t>(n_q) * splits * (hd + 2) * sizeof(float) +
+    const AttnPlan pl = attention_plan(n_q, n_kv, hd, ctx);
+    return 256 + static_cast<size_t>(n_q) * pl.records * (hd + 4) * sizeof(float) +
            static_cast<size_t>(n_kv) * sizeof(unsigned);
 }
 
@@ -718,17 +1187,15 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     const int G = n_q / n_kv;
     if (hd <= 0 || hd % 8 != 0 || hd > 256)
         return set_error(kErrArg, "head_dim=%d must be a multiple of 8 in [8, 256]", hd);
-    const bool tensor = (hd == 64 || hd == 128 || hd == 256) && (G == 1 || G == 2 || G == 4 || G == 8);
-    if (!tensor && G != 1 && G != 2 && G != 4)
+    if (ctx <= 0) return set_error(kErrArg, "context length %d must be positive", ctx);
+    const AttnPlan pl = attention_plan(n_q, n_kv, hd, ctx);
+    if (pl.kind == AttnPlan::kSimt && G != 1 && G != 2 && G != 4)
         return set_error(kErrUnsupported,
                          "query heads per KV head %d (supported: 1, 2, 4; 8 with head_dim 64, 128 or 256)", G);
-    if (ctx <= 0) return set_error(kErrArg, "context length %d must be positive", ctx);
     if (ctx_cap < ctx) return set_error(kErrArg, "cache capacity %d below the context length %d", ctx_cap, ctx);
-    if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) |
-         reinterpret_cast<uintptr_t>(q)) % 16 != 0)
-        return set_error(kErrArg, "q and the K/V caches must be 16-byte aligned");
-    int splits, tpc;
-    attention_plan(n_kv, hd, ctx, &splits, &tpc);
+    if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc) | reinterpret_cast<uintptr_t>(q) |
+         reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+        return set_error(kErrArg, "q, out and the K/V caches must be 16-byte aligned");
     const size_t need = attention_workspace_bytes(n_q, n_kv, hd, ctx);
     if (!ws) return set_error(kErrArg, "attention workspace missing");
     if (ws_bytes < need)
@@ -747,39 +1214,51 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     p.hd = hd;
     p.ctx = ctx;
     p.ctx_cap = ctx_cap;
-    p.splits = splits;
-    p.tpc = tpc;
+    p.splits = pl.splits;
+    p.tpc = pl.tpc;
     p.tt = attention_subtile(hd);
     p.scale_log2 = scale * kLog2e;
-    const size_t wts = static_cast<size_t>(G) * splits * sizeof(float);
+    p.pitch = hd + 4;
+    // scratch of the final merge: staged records (when they fit) or (m, l), weights and group sums
+    const size_t merge_min = ((static_cast<size_t>(G) * pl.records * 12 + 15) & ~size_t(15)) + kAttThreads * 16;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(splits, n_kv, 1);
+    cfg.gridDim = dim3(pl.splits, n_kv, 1);
     cfg.blockDim = dim3(kAttThreads, 1, 1);
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
-    cfg.numAttrs = launch_attrs(attrs, 1);
+    cfg.numAttrs = launch_attrs(attrs, pl.kind == AttnPlan::kSlice ? kFaCluster : 1);
     auto go = [&](auto kern, size_t smem) -> int {
-        if (wts > smem) smem = wts;
+        if (merge_min > smem) smem = merge_min;
         cfg.dynamicSmemBytes = smem;
+        p.smem = static_cast<int>(smem);
         VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
         return kOk;
     };
-    if (tensor) {
+    if (pl.kind == AttnPlan::kSlice) {
         auto pick = [&](auto hd_tag) -> int {
             constexpr int HD = decltype(hd_tag)::value;
-            const size_t smem = MmaGeo<HD>::smem_bytes;
+            const size_t smem = MmaGeo<HD>::ring_bytes + MmaGeo<HD>::q_bytes;
+            cfg.blockDim = dim3(kFaThreads, 1, 1);
             switch (G) {
-                case 1: return go(attention_mma_kernel<1, HD>, smem);
-                case 2: return go(attention_mma_kernel<2, HD>, smem);
-                case 4: return go(attention_mma_kernel<4, HD>, smem);
-                default: return go(attention_mma_kernel<8, HD>, smem);
+                case 1: return go(attention_fa_kernel<1, HD>, smem);
+                case 2: return go(attention_fa_kernel<2, HD>, smem);
+                case 4: return go(attention_fa_kernel<4, HD>, smem);
+                default: return go(attention_fa_kernel<8, HD>, smem);
             }
         };
         if (hd == 64) return pick(std::integral_constant<int, 64>());
-        if (hd == 128) return pick(std::integral_constant<int, 128>());
-        return pick(std::integral_constant<int, 256>());
+        return pick(std::integral_constant<int, 128>());
+    }
+    if (pl.kind == AttnPlan::kMma) {
+        const size_t smem = MmaGeo<256>::smem_bytes;
+        switch (G) {
+            case 1: return go(attention_mma_kernel<1, 256>, smem);
+            case 2: return go(attention_mma_kernel<2, 256>, smem);
+            case 4: return go(attention_mma_kernel<4, 256>, smem);
+            default: return go(attention_mma_kernel<8, 256>, smem);
+        }
     }
     const int chunks = hd / 8;
     size_t smem = static_cast<size_t>(kAttStages) * att_stage_units(p.tt, chunks) * 16 +
