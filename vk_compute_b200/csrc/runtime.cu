@@ -97,7 +97,13 @@ struct Ctx {
     cudaStream_t stream;
     cudaEvent_t ev_begin, ev_end;
     bool timed;
+    // Pinned staging for small writeBuffer uploads: the caller's bytes are
+    // copied here, so the call can return before the device copy has run.
+    void* stage;
+    size_t stage_cap;
+    cudaEvent_t staged;  // recorded after the last upload from `stage`
 };
+constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronously
 constexpr uint32_t kCtxMagic = 0x564b4331u;  // "VKC1"
 
 [[noreturn]] void fatal(const char* fmt, ...) {
@@ -358,7 +364,10 @@ device createDevice() {
     check_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     check_cuda(cudaEventCreate(&c->ev_begin), "cudaEventCreate");
     check_cuda(cudaEventCreate(&c->ev_end), "cudaEventCreate");
+    check_cuda(cudaEventCreateWithFlags(&c->staged, cudaEventDisableTiming), "cudaEventCreate");
     c->timed = false;
+    c->stage = nullptr;
+    c->stage_cap = 0;
     device d;
     d.instance = reinterpret_cast<VkInstance>(c);
     d.device = reinterpret_cast<VkDevice>(c);
@@ -372,6 +381,8 @@ void destroyDevice(device dev) {
     cudaStreamSynchronize(c->stream);
     cudaEventDestroy(c->ev_begin);
     cudaEventDestroy(c->ev_end);
+    cudaEventDestroy(c->staged);
+    if (c->stage) cudaFreeHost(c->stage);
     cudaStreamDestroy(c->stream);
     c->magic = 0;
     delete c;
@@ -431,14 +442,31 @@ void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* outpu
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
 }
 
+// Uploads of up to kStageMax bytes go through the pinned staging buffer and
+// return once the bytes are staged (the caller may reuse `data` at once); the
+// device copy is ordered before every later operation on the session stream.
+// Larger uploads are copied synchronously.
 void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
     Ctx* c = ctx_of(dev);
     if (!buf.buffer) fatal("writeBuffer: empty buffer");
-    if (buf.size > 0)
-        check_cuda(cudaMemcpyAsync(buf.buffer, data, static_cast<size_t>(buf.size),
-                                   cudaMemcpyHostToDevice, c->stream),
-                   "cudaMemcpyAsync");
-    check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    const size_t n = static_cast<size_t>(buf.size);
+    if (n == 0) return;
+    if (n > kStageMax) {
+        check_cuda(cudaMemcpyAsync(buf.buffer, data, n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
+        check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+        return;
+    }
+    check_cuda(cudaEventSynchronize(c->staged), "cudaEventSynchronize");  // previous upload has left `stage`
+    if (c->stage_cap < n) {
+        if (c->stage) check_cuda(cudaFreeHost(c->stage), "cudaFreeHost");
+        c->stage = nullptr;
+        c->stage_cap = 0;
+        check_cuda(cudaHostAlloc(&c->stage, kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
+        c->stage_cap = kStageMax;
+    }
+    memcpy(c->stage, data, n);
+    check_cuda(cudaMemcpyAsync(buf.buffer, c->stage, n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
+    check_cuda(cudaEventRecord(c->staged, c->stream), "cudaEventRecord");
 }
 
 void destroyBuffer(VkDevice dev, buffer buf) {
@@ -448,13 +476,17 @@ void destroyBuffer(VkDevice dev, buffer buf) {
 }
 
 // --- dispatch.h ------------------------------------------------------------
+// The operations are enqueued on the session stream and execute() returns
+// without waiting: their results reach the host only through readBuffer or
+// getExecutionTime, which wait for the stream (and destroyBuffer waits before
+// freeing), so the program sees the same values as with the reference's
+// wait-on-fence execute (src/dispatch.c:8-61) at one host round trip less.
 void execute(session s, operation ops[], int opCount) {
     Ctx* c = ctx_of(s.dev.device);
     if (opCount < 0) fatal("execute: negative operation count");
     check_cuda(cudaEventRecord(c->ev_begin, c->stream), "cudaEventRecord");
     for (int i = 0; i < opCount; ++i) run_op(c, ops[i]);
     check_cuda(cudaEventRecord(c->ev_end, c->stream), "cudaEventRecord");
-    check_cuda(cudaStreamSynchronize(c->stream), "execute");
     check_cuda(cudaGetLastError(), "execute");
     c->timed = true;
 }
@@ -462,6 +494,7 @@ void execute(session s, operation ops[], int opCount) {
 double getExecutionTime(session s) {
     Ctx* c = ctx_of(s.dev.device);
     if (!c->timed) return 0.0;
+    check_cuda(cudaEventSynchronize(c->ev_end), "getExecutionTime");
     float ms = 0.f;
     check_cuda(cudaEventElapsedTime(&ms, c->ev_begin, c->ev_end), "cudaEventElapsedTime");
     return static_cast<double>(ms);
