@@ -144,6 +144,26 @@ int vkc_attention_decode_noalloc(const void* q, int q_bits, const void* kcache, 
 /* C = A B, row-major fp32 (A M x K, B K x N).  Replaces shader/gemm.comp. */
 int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, void* stream);
 
+/* ---- exchange between the GPUs of one node (row-sharded decoder chain) ----
+ * No counterpart in the reference (which runs on one GPU).  All-gather of an
+ * fp32 vector whose rank-r slice (slice_floats values) is `src`: the slice is
+ * stored over NVLink into every rank's full buffer at offset r*slice_floats.
+ * dsts (device array of `world` pointers) are the ranks' full buffers and
+ * counters (device array of `world` pointers) the ranks' arrival counters
+ * (world unsigned each, zero before the first launch), all mapped into this
+ * process (CUDA IPC).  Every rank makes the same sequence of launches; a launch
+ * returns on the GPU once every rank's slice has arrived here.  A wait that
+ * exceeds its bound sets bit 8 in *status (device memory) instead of hanging. */
+int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats,
+                      int rank, int world, unsigned* status, void* stream);
+/* Peer memory for the above: a zeroed device allocation of `bytes` and its
+ * 64-byte CUDA IPC handle; open maps a peer's handle into the current device
+ * (peer access enabled on first use); close unmaps; free releases. */
+int vkc_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int vkc_ipc_open(const void* handle, void** ptr);
+int vkc_ipc_close(void* ptr);
+int vkc_ipc_free(void* ptr);
+
 /* ---- weight preparation on the GPU (bit-identical to src/data.c) ---- */
 
 /* dst[r*N + c] = get_pseudo_random(r, c, seed) (src/data.c:8-28); fp32 when

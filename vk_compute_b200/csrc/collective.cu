@@ -1,0 +1,153 @@
+// All-gather of fp32 slices between the GPUs of one node by direct NVLink
+// stores into the peers' memory: the exchange step of the row-sharded decoder
+// chain (each rank owns a contiguous slice of an activation vector and every
+// rank needs the whole vector).
+//
+// The full buffers and the arrival counters of every rank are mapped into
+// every other rank's address space (CUDA IPC; plain peer memory, no NVLink
+// multicast objects).  A launch copies this rank's slice into every rank's
+// buffer at offset rank * slice; after a CTA barrier one thread makes the
+// stores visible system-wide with a single fence, adds one to this rank's
+// counter slot on every rank (relaxed, system scope), and waits (relaxed
+// polling, bounded, then a fence) until every rank's slot in this rank's
+// counters has reached this launch's target.  One fence per launch instead of
+// one per thread or per atomic: measured 6-7 us per gather on two B200s in a
+// CUDA graph, against 16-18 us with release atomics and per-thread fences and
+// 21-23 us for NCCL's all-gather.  Counters only grow: with a fixed number of
+// CTAs per launch, the k-th launch of a rank targets k * kGatherCtas, which
+// each CTA derives from the value its own increment of its own slot returned,
+// so captured graphs can be replayed without resetting anything.  All ranks
+// must make the same sequence of launches.  A wait that runs out sets bit
+// kStatusPeerTimeout in the caller's status word and returns.
+#include "vkc_common.cuh"
+
+#include <cstring>
+
+namespace vkc {
+namespace {
+
+constexpr int kGatherCtas = 1;
+constexpr int kGatherThreads = 512;
+constexpr unsigned kStatusPeerTimeout = 8u;
+
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned atom_add_relaxed_sys(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.relaxed.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kGatherThreads) allgather_kernel(const float4* __restrict__ src,
+                                                                   float* const* dsts, unsigned* const* ctrs,
+                                                                   int slice4, int rank, int world,
+                                                                   unsigned* status) {
+    pdl_launch_dependents();
+    pdl_wait();  // the slice comes from the previous kernel
+    const int stride = gridDim.x * blockDim.x;
+    for (int p = 0; p < world; ++p) {
+        float4* d = reinterpret_cast<float4*>(dsts[p]) + static_cast<size_t>(rank) * slice4;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slice4; i += stride) d[i] = src[i];
+    }
+    __syncthreads();  // the CTA's stores, ordered before thread 0's fence below
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();  // release: the slice stores before the arrivals
+        unsigned target = 0;
+        for (int p = 0; p < world; ++p) {
+            if (p == rank) {
+                const unsigned old = atom_add_relaxed_sys(ctrs[p] + rank, 1u);
+                target = (old / gridDim.x + 1) * gridDim.x;
+            } else {
+                red_add_relaxed_sys(ctrs[p] + rank, 1u);
+            }
+        }
+        const unsigned* mine = ctrs[rank];
+        bool ok = true;
+        for (int q = 0; q < world && ok; ++q) {
+            uint32_t it = 0;
+            while (static_cast<int>(ld_relaxed_sys(mine + q) - target) < 0) {
+                if (++it > kSpinLimit) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        fence_acq_rel_sys();  // acquire: the peers' slices after their arrivals
+        if (!ok) atomicOr(status, kStatusPeerTimeout);
+    }
+    __syncthreads();
+}
+
+}  // namespace
+}  // namespace vkc
+
+using namespace vkc;
+
+extern "C" {
+
+int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats, int rank,
+                      int world, unsigned* status, void* stream) {
+    if (!src || !dsts || !counters || !status) return set_error(kErrArg, "null all-gather pointer");
+    if (world < 1 || rank < 0 || rank >= world) return set_error(kErrArg, "rank %d of world %d", rank, world);
+    if (slice_floats <= 0 || slice_floats % 4 != 0)
+        return set_error(kErrArg, "slice of %d floats (must be a positive multiple of 4)", slice_floats);
+    if (reinterpret_cast<uintptr_t>(src) % 16 != 0) return set_error(kErrArg, "source must be 16-byte aligned");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kGatherCtas, 1, 1);
+    cfg.blockDim = dim3(kGatherThreads, 1, 1);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[2];
+    cfg.attrs = attrs;
+    cfg.numAttrs = launch_attrs(attrs, 1);
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, allgather_kernel, reinterpret_cast<const float4*>(src),
+                                    reinterpret_cast<float* const*>(dsts), counters, slice_floats / 4, rank, world,
+                                    status));
+    return kOk;
+}
+
+// ---- peer memory: one allocation per rank, shared through CUDA IPC --------
+
+int vkc_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return set_error(kErrArg, "vkc_ipc_alloc: null pointer or zero size");
+    void* p = nullptr;
+    VKC_CUDA_TRY(cudaMalloc(&p, bytes));
+    VKC_CUDA_TRY(cudaMemset(p, 0, bytes));
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return set_error(kErrCuda, "cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
+    }
+    memcpy(handle, &h, sizeof h);
+    *ptr = p;
+    return kOk;
+}
+
+// Maps a peer's allocation into the current device's context (peer access is
+// enabled on first use).
+int vkc_ipc_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return set_error(kErrArg, "vkc_ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    VKC_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return kOk;
+}
+
+int vkc_ipc_close(void* ptr) {
+    VKC_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return kOk;
+}
+
+int vkc_ipc_free(void* ptr) {
+    VKC_CUDA_TRY(cudaFree(ptr));
+    return kOk;
+}
+
+}  // extern "C"

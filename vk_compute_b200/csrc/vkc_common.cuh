@@ -130,7 +130,7 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
     return pol;
 }
 // Global -> shared bulk copy completing on an mbarrier (16-byte aligned
-// addresses, size a multiple of 16).  No multicast.
+// addresses, size a multiple of 16).  Single-destination copies only.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
                                          uint64_t policy) {
     asm volatile(

@@ -19,7 +19,8 @@ Sharding over `world` GPUs of one node (one process each): rank r owns query
 heads [r*nq/world, (r+1)*nq/world) and the matching KV heads, so QKV,
 RoPE, the cache and attention are local; the O, gate/up and down projections
 are split by output rows.  Four all-gathers per layer assemble the attention
-output, x', h and x'' from the ranks' slices.
+output, x', h and x'' from the ranks' slices (NVLink peer stores by default,
+NCCL on request).
 """
 from __future__ import annotations
 
@@ -170,25 +171,40 @@ class ShardedDecoder:
 
     `step(pos)` advances the hidden state `buf.x` by one token at position
     `pos` (attending to tokens [0, pos]) and returns it.  With world > 1 the
-    all-gathers run through torch.distributed (NCCL) on the current stream, so
-    a step can be captured in a CUDA graph.
+    four all-gathers per layer run on the current stream either as the
+    library's NVLink peer all-gather (exchange="p2p", the default: the full
+    buffers live in peer-mapped memory, see p2p.PeerGather) or through
+    torch.distributed (exchange="nccl"); either way a step can be captured in a
+    CUDA graph.  Call close() before the process group is destroyed.
     """
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
-                 group=None, layers: list[LayerShard] | None = None):
+                 group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p"):
         self.cfg = cfg
         self.plan = shard_plan(cfg, rank, world)
         self.device = torch.device(device or "cuda")
         self.group = group
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange {exchange!r} (expected 'p2p' or 'nccl')")
+        self.exchange = exchange if world > 1 else "none"
         self.layers = layers if layers is not None else [
             build_layer(cfg, self.plan, i, self.device, seed) for i in range(cfg.layers)]
         self.theta = rope_theta(cfg, self.device)
         H, I, hd = cfg.hidden, cfg.inter, cfg.head_dim
         p = self.plan
         z = lambda n: torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.peer = None
+        full = {"x": H, "x_mid": H, "attn_full": cfg.n_q * hd, "h_full": I}
+        if self.exchange == "p2p":
+            from .p2p import PeerGather
+
+            self.peer = PeerGather(full, self.device, group)
+            fb = self.peer.buffers
+        else:
+            fb = {n: z(k) for n, k in full.items()}
         self.buf = Buffers(
-            x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd), attn_full=z(cfg.n_q * hd),
-            o_slice=z(p.o_rows[1] - p.o_rows[0]), h=z(p.ffn_rows[1] - p.ffn_rows[0]), h_full=z(I),
+            x=fb["x"], x_mid=fb["x_mid"], qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd), attn_full=fb["attn_full"],
+            o_slice=z(p.o_rows[1] - p.o_rows[0]), h=z(p.ffn_rows[1] - p.ffn_rows[0]), h_full=fb["h_full"],
             d_slice=z(p.o_rows[1] - p.o_rows[0]),
             ws=ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device))
 
@@ -201,14 +217,23 @@ class ShardedDecoder:
         kv = 2 * (pos + 1) * p.n_kv * cfg.head_dim * 2
         return n + cfg.layers * kv
 
-    def _gather(self, out: torch.Tensor, part: torch.Tensor) -> None:
-        if self.plan.world == 1:
+    def _gather(self, name: str, part: torch.Tensor) -> None:
+        out = getattr(self.buf, name)
+        if self.exchange == "none":
             if out.data_ptr() != part.data_ptr():
                 out.copy_(part)
-            return
-        import torch.distributed as dist
+        elif self.exchange == "p2p":
+            self.peer.gather(name, part)
+        else:
+            import torch.distributed as dist
 
-        dist.all_gather_into_tensor(out, part, group=self.group)
+            dist.all_gather_into_tensor(out, part, group=self.group)
+
+    def close(self) -> None:
+        """Releases the peer-mapped buffers (collective over the group)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def step(self, pos: int) -> torch.Tensor:
         cfg, p, b = self.cfg, self.plan, self.buf
@@ -225,17 +250,17 @@ class ShardedDecoder:
             ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
                                  workspace=b.ws, out=b.attn_full if single else b.attn, ctx_cap=cfg.ctx)
             if not single:
-                self._gather(b.attn_full, b.attn)
+                self._gather("attn_full", b.attn)
             ops.gemv_residual(L.o, b.attn_full, b.x[o0:o1], out=b.x_mid if single else b.o_slice)
             if not single:
-                self._gather(b.x_mid, b.o_slice)
+                self._gather("x_mid", b.o_slice)
             ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h_full if single else b.h)
             if not single:
-                self._gather(b.h_full, b.h)
+                self._gather("h_full", b.h)
             ops.gemv_residual(L.down, b.h_full, b.x_mid[o0:o1], out=b.x if single else b.d_slice)
             if not single:
-                self._gather(b.x, b.d_slice)
+                self._gather("x", b.d_slice)
         return b.x
 
     def kernels_per_step(self) -> int:
-        return 5 * self.cfg.layers
+        return (9 if self.exchange == "p2p" else 5) * self.cfg.layers
