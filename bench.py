@@ -49,6 +49,7 @@ WORKLOADS = {
     "gemv_fp16": "GEMV FP16 4096x4096 (x 4096)",
     "swiglu_ffn_int4": "RmsNorm-swiglu-ffn INT4 gate/up 12288x4096 + down GEMV INT4 4096x12288",
     "qkv_rope_attn_int4": "RmsNorm-GEMV-Rope INT4 QKV 6144x4096 (theta 1e6) + Att-full-FP16 32q/8kv x 128, ctx 8192",
+    "prefill_gemm_bf16": "prefill GEMM bf16 on tcgen05: A 64x4096 . W^T (W 12288x4096, K-major) -> C 64x12288 fp32",
 }
 
 
@@ -58,6 +59,13 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text()).get("bf16_tflops", 1590.0))
+    return 1590.0
 
 
 def ncu_traffic(workload: str):
@@ -240,6 +248,20 @@ def build_workload(name: str, rank: int, device):
         return dict(step=step, bytes=wbytes + kvbytes + act, launches=2, dominant=dom,
                     dominant_bytes=kvbytes + 4 * NQ * HD * 2, dominant_name="Att-full-FP16",
                     meta={"pool": n, "pos": pos, "ctx": CTX}, e2e=None)
+    if name == "prefill_gemm_bf16":
+        M, N, K = 64, 12288, 4096
+        a = randn(M, K).to(torch.bfloat16)
+        c = torch.empty(M, N, device=device)
+        wbytes = N * K * 2
+        n = max(2, min(16, math.ceil(4 * L2_BYTES / wbytes)))
+        base = [randn(N, K, std=0.02).to(torch.bfloat16) for _ in range(2)]
+        ws = [base[j] if j < 2 else base[j % 2].clone() for j in range(n)]
+        step = lambda i: ops.gemm_bf16(a, ws[i % n], out=c)
+        nbytes = wbytes + M * K * 2 + M * N * 4
+        return dict(step=step, bytes=nbytes, launches=1, dominant=step, dominant_bytes=nbytes,
+                    dominant_name="gemm_tc_kernel (tcgen05, bf16)", meta={"M": M, "N": N, "K": K, "pool": n,
+                                                                          "flop": 2 * M * N * K},
+                    e2e=None)
     raise SystemExit(f"unknown workload {name}; choose from {sorted(WORKLOADS)}")
 
 
@@ -391,6 +413,23 @@ def cpu_baseline(workload: str, budget_s: float = 12.0, threads: int | None = No
     threads = threads or len(os.sched_getaffinity(0))
     o.set_threads(threads)
     rng = np.random.default_rng(0)
+    if workload == "prefill_gemm_bf16":
+        # gemm.comp's arithmetic (the oracle's restatement) on a column slice
+        M, K, Ns = 64, 4096, 1536
+        a = rng.standard_normal((M, K), dtype=np.float32)
+        b = rng.standard_normal((K, Ns), dtype=np.float32) * 0.02
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            o.gemm(a, b)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 200:
+                break
+        per = el / reps
+        nbytes = K * Ns * 2 + M * K * 2 + M * Ns * 4
+        return {"value": round(nbytes / per / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{reps} passes of 64x4096 . 4096x{Ns} (1/8 of the columns) in {el:.1f} s",
+                "s_per_pass": per}
     if workload == "rmsnorm_gemv_int8":
         K, N, bits = 4096, 12288, 8
     elif workload == "gemv_fp16":
@@ -438,6 +477,17 @@ def run_reference(args, rank, world):
     wl = args.workload
     threads = len(os.sched_getaffinity(0))
     o.set_threads(threads)
+    if wl == "prefill_gemm_bf16":
+        r = cpu_baseline(wl, budget_s=max(1.0, 0.5 * args.steps), threads=threads)
+        line = {"impl": "reference", "metric": f"{WORKLOADS[wl]} achieved HBM GB/s", "value": r["value"],
+                "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(r["s_per_pass"] * 8e3, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": wl, "description": WORKLOADS[wl]},
+                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     K, N, bits = {"rmsnorm_gemv_int8": (4096, 12288, 8), "gemv_fp16": (4096, 4096, 16),
                   "swiglu_ffn_int4": (4096, 12288, 4), "qkv_rope_attn_int4": (4096, 6144, 4)}[wl]
     rng = np.random.default_rng(0)
@@ -612,6 +662,9 @@ def main():
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes": wl["dominant_bytes"],
                          "us_per_launch": round(dom_s * 1e6, 3)},
+            "tensor": ({"achieved_tflops": round(wl["meta"]["flop"] / dom_s / 1e12, 2),
+                        "peak_tflops": tensor_peak(), "frac": round(wl["meta"]["flop"] / dom_s / 1e12 / tensor_peak(), 4)}
+                       if "flop" in wl["meta"] else None),
             "gpu_launches": args.steps * wl["launches"],
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -164,6 +164,16 @@ int vkc_ipc_open(const void* handle, void** ptr);
 int vkc_ipc_close(void* ptr);
 int vkc_ipc_free(void* ptr);
 
+/* Prefill GEMM on the tcgen05 tensor cores: C[M][N] (fp32) = A[M][K] (bf16)
+ * . W[N][K]^T (bf16); A and W row-major, so W is the K-major (N rows of K)
+ * layout of a linear layer's weight.  The batched form of gemm.comp's
+ * contraction (shader/gemm.comp:19-59) for prefill.  K a multiple of 64, N a
+ * multiple of 96, any M (tiles of 128 rows).  Pointers 16-byte aligned. */
+int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, void* stream);
+/* Status bits of vkc_gemm_bf16 on the current device (16: a bounded wait ran
+ * out); waits for the device; `clear` resets them. */
+int vkc_gemm_bf16_status(unsigned* status, int clear);
+
 /* ---- weight preparation on the GPU (bit-identical to src/data.c) ---- */
 
 /* dst[r*N + c] = get_pseudo_random(r, c, seed) (src/data.c:8-28); fp32 when

@@ -32,6 +32,8 @@ SIGNATURES = {
     "vkc_attention_decode": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_attention_decode_cache": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_gemm_f32": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "vkc_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "vkc_gemm_bf16_status": (_i, [C.POINTER(C.c_uint), _i]),
     "vkc_generate": (_i, [_i, _i, _i, _i, _p, _p]),
     "vkc_quantize": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p]),
     "vkc_pack_block16": (_i, [_p, _p, _i, _i, _i, _p]),

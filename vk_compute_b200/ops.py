@@ -211,5 +211,26 @@ def gemm_f32(a: torch.Tensor, b: torch.Tensor, out=None, stream=None) -> torch.T
     return c
 
 
+def gemm_bf16(a: torch.Tensor, w: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    """C = A W^T on the tcgen05 tensor cores: A [M, K] and W [N, K] bf16
+    (contiguous), C [M, N] fp32."""
+    if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise TypeError("gemm_bf16 takes bf16 A and W")
+    a, w = a.contiguous(), w.contiguous()
+    M, K = a.shape
+    N, K2 = w.shape
+    if K != K2:
+        raise ValueError(f"A is {M}x{K} but W is {N}x{K2}")
+    c = torch.empty(M, N, dtype=torch.float32, device=a.device) if out is None else out
+    check(lib().vkc_gemm_bf16(_p(a), _p(w), _p(c), M, N, K, _s(stream)))
+    return c
+
+
+def gemm_bf16_status(clear: bool = True) -> int:
+    v = C.c_uint(0)
+    check(lib().vkc_gemm_bf16_status(C.byref(v), int(clear)))
+    return v.value
+
+
 def set_pdl(enable: bool) -> None:
     lib().vkc_set_pdl(int(enable))
