@@ -33,9 +33,11 @@ typedef struct operation {
 } operation;
 
 /* include/dispatch.h:25 -- launch ops[0..opCount) in order on the session
- * stream, then wait for completion (src/dispatch.c:8-61).  Unknown operator
- * names, missing bindings and undersized buffers print to stderr and exit,
- * as the reference does on its fatal paths. */
+ * stream (src/dispatch.c:8-61).  Returns once the work is enqueued: results
+ * reach the host only through readBuffer / getExecutionTime, which wait for
+ * the stream, so a caller sees what the reference's wait-on-fence execute
+ * gives.  Unknown operator names, missing bindings and undersized buffers
+ * print to stderr and exit, as the reference does on its fatal paths. */
 void execute(session s, operation ops[], int opCount);
 /* include/dispatch.h:26 -- device time of the last execute, in ms. */
 double getExecutionTime(session s);

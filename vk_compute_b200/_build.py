@@ -22,6 +22,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 OBJ = PKG / "_build"
 LIB = PKG / "libvkcompute.so"
+E2E_BIN = PKG / "vkc_e2e_bench"
 ORACLE = ROOT / "oracle"
 ORACLE_LIB = ORACLE / "liboracle.so"
 REFERENCE = Path(os.environ.get("VKC_REFERENCE", "/root/reference"))
@@ -82,6 +83,15 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+def build_e2e(force: bool = False) -> Path:
+    """The C end-to-end timing host (csrc/e2e_bench.c) against libvkcompute."""
+    src = CSRC / "e2e_bench.c"
+    if force or _stale(E2E_BIN, [src, LIB]):
+        _run(["gcc", "-O2", "-Wall", f"-I{INCLUDE / 'vkshim'}", f"-I{INCLUDE}", "-o", str(E2E_BIN), str(src),
+              f"-L{PKG}", "-lvkcompute", "-Wl,-rpath,$ORIGIN"])
+    return E2E_BIN
+
+
 def build_oracle(force: bool = False) -> Path:
     src = ORACLE / "oracle.c"
     if force or _stale(ORACLE_LIB, [src, ORACLE / "oracle.h"]):
@@ -104,6 +114,7 @@ def build_reference(force: bool = False) -> bool:
 
 def build_all(force: bool = False, with_ref: bool = True, verbose: bool = False) -> None:
     build_library(force=force, verbose=verbose)
+    build_e2e(force=force)
     build_oracle(force=force)
     if with_ref:
         build_reference(force=force)

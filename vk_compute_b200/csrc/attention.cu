@@ -1232,7 +1232,7 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
         if (merge_min > smem) smem = merge_min;
         cfg.dynamicSmemBytes = smem;
         p.smem = static_cast<int>(smem);
-        VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
         VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
         return kOk;
     };

@@ -293,7 +293,7 @@ int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, v
     VKC_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_tc_status));
     auto kern = gemm_tc_kernel<BN>;
     const size_t smem = TcGeo<BN>::smem_bytes;
-    VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(N / BN, (M + kBM - 1) / kBM, 1);
     cfg.blockDim = dim3(kTcThreads, 1, 1);

@@ -507,7 +507,7 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
                          smem);
     auto go = [&](auto kern) -> int {
         if (smem > 48 * 1024)
-            VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+            if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
         cfg.blockDim = dim3(kThreads, 1, 1);

@@ -17,6 +17,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 extern "C" {
 #include "session.h"
@@ -78,6 +79,32 @@ int device_workspace(size_t bytes, void** out, cudaStream_t stream) {
     return kOk;
 }
 
+namespace {
+struct SmemAttr {
+    int dev;
+    const void* func;
+    size_t bytes;
+};
+std::mutex g_attr_mu;
+std::vector<SmemAttr> g_attrs;
+}  // namespace
+
+int ensure_smem(const void* func, size_t bytes) {
+    int dev = 0;
+    VKC_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    for (auto& a : g_attrs)
+        if (a.dev == dev && a.func == func) {
+            if (a.bytes >= bytes) return kOk;
+            VKC_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+            a.bytes = bytes;
+            return kOk;
+        }
+    VKC_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+    g_attrs.push_back({dev, func, bytes});
+    return kOk;
+}
+
 int launch_attrs(cudaLaunchAttribute* attrs, int cluster_x) {
     attrs[0].id = cudaLaunchAttributeClusterDimension;
     attrs[0].val.clusterDim.x = cluster_x < 1 ? 1 : cluster_x;
@@ -99,9 +126,10 @@ struct Ctx {
     bool timed;
     // Pinned staging for small writeBuffer uploads: the caller's bytes are
     // copied here, so the call can return before the device copy has run.
-    void* stage;
-    size_t stage_cap;
-    cudaEvent_t staged;  // recorded after the last upload from `stage`
+    void* stage[2];
+    cudaEvent_t staged[2];  // recorded after the last upload from each slot
+    int next;
+    void* rstage;  // pinned landing buffer for small reads
 };
 constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronously
 constexpr uint32_t kCtxMagic = 0x564b4331u;  // "VKC1"
@@ -364,10 +392,13 @@ device createDevice() {
     check_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     check_cuda(cudaEventCreate(&c->ev_begin), "cudaEventCreate");
     check_cuda(cudaEventCreate(&c->ev_end), "cudaEventCreate");
-    check_cuda(cudaEventCreateWithFlags(&c->staged, cudaEventDisableTiming), "cudaEventCreate");
+    for (int i = 0; i < 2; ++i) {
+        check_cuda(cudaEventCreateWithFlags(&c->staged[i], cudaEventDisableTiming), "cudaEventCreate");
+        c->stage[i] = nullptr;
+    }
+    c->next = 0;
+    c->rstage = nullptr;
     c->timed = false;
-    c->stage = nullptr;
-    c->stage_cap = 0;
     device d;
     d.instance = reinterpret_cast<VkInstance>(c);
     d.device = reinterpret_cast<VkDevice>(c);
@@ -381,8 +412,11 @@ void destroyDevice(device dev) {
     cudaStreamSynchronize(c->stream);
     cudaEventDestroy(c->ev_begin);
     cudaEventDestroy(c->ev_end);
-    cudaEventDestroy(c->staged);
-    if (c->stage) cudaFreeHost(c->stage);
+    for (int i = 0; i < 2; ++i) {
+        cudaEventDestroy(c->staged[i]);
+        if (c->stage[i]) cudaFreeHost(c->stage[i]);
+    }
+    if (c->rstage) cudaFreeHost(c->rstage);
     cudaStreamDestroy(c->stream);
     c->magic = 0;
     delete c;
@@ -432,13 +466,22 @@ void createTransferAndCopy(VkDevice dev, VkQueue, buffer*, int) {
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
 }
 
+// Reads of up to kStageMax bytes land in a pinned staging buffer and are
+// copied out on the host (a direct copy into pageable memory takes the
+// driver's slower pageable path); larger reads copy directly.
 void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* output) {
     Ctx* c = ctx_of(dev);
     if (!buf.buffer) fatal("readBuffer: empty buffer");
-    if (buf.size > 0)
-        check_cuda(cudaMemcpyAsync(output, buf.buffer, static_cast<size_t>(buf.size),
-                                   cudaMemcpyDeviceToHost, c->stream),
-                   "cudaMemcpyAsync");
+    const size_t n = static_cast<size_t>(buf.size);
+    if (n > 0 && n <= kStageMax) {
+        if (!c->rstage) check_cuda(cudaHostAlloc(&c->rstage, kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
+        check_cuda(cudaMemcpyAsync(c->rstage, buf.buffer, n, cudaMemcpyDeviceToHost, c->stream), "cudaMemcpyAsync");
+        check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+        memcpy(output, c->rstage, n);
+        return;
+    }
+    if (n > 0)
+        check_cuda(cudaMemcpyAsync(output, buf.buffer, n, cudaMemcpyDeviceToHost, c->stream), "cudaMemcpyAsync");
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
 }
 
@@ -456,17 +499,16 @@ void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
         check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
         return;
     }
-    check_cuda(cudaEventSynchronize(c->staged), "cudaEventSynchronize");  // previous upload has left `stage`
-    if (c->stage_cap < n) {
-        if (c->stage) check_cuda(cudaFreeHost(c->stage), "cudaFreeHost");
-        c->stage = nullptr;
-        c->stage_cap = 0;
-        check_cuda(cudaHostAlloc(&c->stage, kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
-        c->stage_cap = kStageMax;
-    }
-    memcpy(c->stage, data, n);
-    check_cuda(cudaMemcpyAsync(buf.buffer, c->stage, n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
-    check_cuda(cudaEventRecord(c->staged, c->stream), "cudaEventRecord");
+    // Two staging slots used in turn: a slot is reused only after the upload
+    // before last has left it (normally long done).
+    const int slot = c->next;
+    c->next ^= 1;
+    if (cudaEventQuery(c->staged[slot]) != cudaSuccess)
+        check_cuda(cudaEventSynchronize(c->staged[slot]), "cudaEventSynchronize");
+    if (!c->stage[slot]) check_cuda(cudaHostAlloc(&c->stage[slot], kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
+    memcpy(c->stage[slot], data, n);
+    check_cuda(cudaMemcpyAsync(buf.buffer, c->stage[slot], n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
+    check_cuda(cudaEventRecord(c->staged[slot], c->stream), "cudaEventRecord");
 }
 
 void destroyBuffer(VkDevice dev, buffer buf) {

@@ -45,6 +45,11 @@ constexpr size_t kWorkspaceHeader = 256;
 // number of attributes written into attrs[0..2).
 int launch_attrs(cudaLaunchAttribute* attrs, int cluster_x);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `func` on the current
+// device, skipped when an equal or larger value was already set (the call
+// costs microseconds of host time on every launch otherwise).
+int ensure_smem(const void* func, size_t bytes);
+
 // ---------------------------------------------------------------------------
 // Device helpers
 // ---------------------------------------------------------------------------
