@@ -345,9 +345,10 @@ def e2e_dropin(args, e2e, device_index):
 def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float):
     """The 36-layer decoder chain (hidden 4096, 32 query / 8 KV heads of 128,
     intermediate 12288, int4 weights ~N(0,0.02), random-init) for one token at
-    position 8191 (attention over a full 8192-token fp16 cache), row-sharded
-    over `world` GPUs with four all-gathers per layer (the library's NVLink
-    peer all-gather).  Steps are graph launches; time is the max over ranks."""
+    position 8191 (attention over a full 8192-token fp16 cache), sharded over
+    `world` GPUs by heads (QKV, attention), input rows (O, down) and output
+    rows (gate/up) with two all-reduces per layer (the library's NVLink peer
+    all-reduce).  Steps are graph launches; time is the max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -395,9 +396,9 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
     return {"layers": cfg.layers, "us_per_step": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
             "bytes_per_step": rank_bytes * world, "GB_s": round(rank_bytes * world / us / 1e3, 1),
             "frac_of_peak_per_gpu": round(rank_bytes / us / 1e3 / peak, 4),
-            "kernels_per_step": kernels, "all_gathers_per_step": 4 * cfg.layers if world > 1 else 0,
+            "kernels_per_step": kernels, "all_reduces_per_step": 2 * cfg.layers if world > 1 else 0,
             "steps": steps, "warmup": warmup, "pos": pos, "ctx": cfg.ctx,
-            "parallelism": (f"row/head shards x{world}, all-gather x4 per layer ({exchange}: "
+            "parallelism": (f"head/K-split shards x{world}, all-reduce x2 per layer ({exchange}: "
                             + ("NVLink peer stores" if exchange == "p2p" else "NCCL") + ")") if world > 1 else "1 GPU",
             "build_s": round(build_s, 1),
             "model": "36 x (RmsNorm-GEMV-Rope QKV 6144x4096 + KV append, Att-full GQA 32/8 x 128, "

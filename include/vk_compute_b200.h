@@ -156,6 +156,14 @@ int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, 
  * exceeds its bound sets bit 8 in *status (device memory) instead of hanging. */
 int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats,
                       int rank, int world, unsigned* status, void* stream);
+/* All-reduce with residual for K-split projections (no counterpart in the
+ * reference): `part` is this rank's partial output (n floats); it is stored
+ * into slot `rank` of every rank's partial buffer (slots: device array of
+ * `world` pointers to [world][n] floats), and once every rank's slot has
+ * arrived (same counters and protocol as vkc_allgather_p2p) each rank writes
+ * out = residual + sum of the slots in rank order (out must not alias part). */
+int vkc_allreduce_residual_p2p(const float* part, void* const* slots, unsigned* const* counters, int n, int rank,
+                               int world, const float* residual, float* out, unsigned* status, void* stream);
 /* Peer memory for the above: a zeroed device allocation of `bytes` and its
  * 64-byte CUDA IPC handle; open maps a peer's handle into the current device
  * (peer access enabled on first use); close unmaps; free releases. */

@@ -1,7 +1,7 @@
 """Host logic of the sharded decoder (no GPU): the shard plan covers every
 head and row exactly once, keeps quantised shards on 256-row scale blocks,
-and the rank-ordered all-gather the decoder relies on reassembles slices in
-plan order (two gloo ranks on CPU)."""
+and the K-split projections summed over ranks (the all-reduce the decoder
+relies on) reproduce the unsharded product (two gloo ranks on CPU)."""
 import os
 
 import pytest
@@ -19,7 +19,8 @@ def test_plan_partitions_heads_and_rows(world):
     qkv = sorted(c for p in plans for c in p.qkv_cols)
     assert qkv == list(range(cfg.qkv_rows))
     assert [p.q_heads for p in plans] == [(r * 32 // world, (r + 1) * 32 // world) for r in range(world)]
-    assert sum(p.o_rows[1] - p.o_rows[0] for p in plans) == cfg.hidden
+    assert [p.o_k for p in plans] == [(r * cfg.n_q * cfg.head_dim // world, (r + 1) * cfg.n_q * cfg.head_dim // world)
+                                      for r in range(world)]
     assert sum(p.ffn_rows[1] - p.ffn_rows[0] for p in plans) == cfg.inter
     for p in plans:
         hd = cfg.head_dim
@@ -42,25 +43,34 @@ def test_plan_rejects_uneven_splits():
         shard_plan(DecoderConfig(hidden=1024, inter=1536, n_q=8, n_kv=8), 0, 8)  # 128-row int4 shards
 
 
-def _gather_worker(rank, world, port, q):
+def _ksplit_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg = DecoderConfig()
+        cfg = DecoderConfig(hidden=512, inter=1024, n_q=8, n_kv=2, head_dim=64, bits=16)
         p = shard_plan(cfg, rank, world)
-        part = torch.arange(p.o_rows[0], p.o_rows[1], dtype=torch.float32)
-        full = torch.empty(cfg.hidden, dtype=torch.float32)
-        dist.all_gather_into_tensor(full, part)
-        q.put((rank, bool(torch.equal(full, torch.arange(cfg.hidden, dtype=torch.float32)))))
+        g = torch.Generator().manual_seed(3)
+        w_o = torch.randn(cfg.n_q * cfg.head_dim, cfg.hidden, generator=g, dtype=torch.float64)
+        w_d = torch.randn(cfg.inter, cfg.hidden, generator=g, dtype=torch.float64)
+        a = torch.randn(cfg.n_q * cfg.head_dim, generator=g, dtype=torch.float64)
+        h = torch.randn(cfg.inter, generator=g, dtype=torch.float64)
+        res = torch.randn(cfg.hidden, generator=g, dtype=torch.float64)
+        (o0, o1), (f0, f1) = p.o_k, p.ffn_rows
+        o = w_o[o0:o1].T @ a[o0:o1]
+        d = w_d[f0:f1].T @ h[f0:f1]
+        dist.all_reduce(o)
+        dist.all_reduce(d)
+        ok = bool(torch.allclose(res + o, res + w_o.T @ a, atol=1e-9)) and bool(torch.allclose(d, w_d.T @ h, atol=1e-9))
+        q.put((rank, ok))
     finally:
         dist.destroy_process_group()
 
 
-def test_rank_ordered_gather_two_gloo_ranks():
+def test_ksplit_allreduce_two_gloo_ranks():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 1000
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ksplit_worker, args=(r, 2, port, q)) for r in range(2)]
     for pr in procs:
         pr.start()
     for pr in procs:

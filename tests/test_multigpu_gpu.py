@@ -1,10 +1,11 @@
 """Two-GPU paths (skipped on a one-GPU box): the NVLink peer all-gather
-against the expected concatenation, replayed from a CUDA graph, and the
-row-sharded decoder chain at world 2 (peer all-gather and NCCL exchanges)
-against the same model on one GPU.  The chain test uses fp16 weights: with
-int4/int8 weights the head-permuted QKV shard is quantised in other 256-row
-scale blocks than the unsharded matrix, so the models differ by quantisation
-rounding (every other projection shards along whole scale blocks)."""
+against the expected concatenation and the peer all-reduce with residual
+against the rank-ordered sum, both eager and replayed from a CUDA graph, and
+the sharded decoder chain at world 2 (peer and NCCL all-reduces) against the
+same model on one GPU.  The chain test uses fp16 weights: with int4/int8
+weights the head-permuted QKV shard is quantised in other 256-row scale
+blocks than the unsharded matrix, so the models differ by quantisation
+rounding (the K-split O and down projections keep their scales exactly)."""
 import os
 import socket
 import tempfile
@@ -43,7 +44,7 @@ def _gather_child(rank, world, port, out_dir):
 
     dev = torch.device("cuda", rank)
     n = 1024
-    pg = PeerGather({"v": n * world, "w": 3 * 256 * world}, dev)
+    pg = PeerGather({"v": n * world, "w": 3 * 256 * world, "r": 2048 * world}, dev)
     ok = True
     part = torch.empty(n, device=dev)
     part2 = torch.empty(3 * 256, device=dev)
@@ -78,7 +79,47 @@ def _gather_child(rank, world, port, out_dir):
         ok &= bool(torch.equal(pg.buffers["v"].cpu(), want))
         want2 = torch.cat([torch.full((3 * 256,), float(-r - it)) for r in range(world)])
         ok &= bool(torch.equal(pg.buffers["w"].cpu(), want2))
+    # all-reduce with residual, interleaved with gathers on the same counters
+    red_part = torch.empty(2048, device=dev)
+    res = torch.empty(2048, device=dev)
+    red_out = torch.empty(2048, device=dev)
+    red_out2 = torch.empty(2048, device=dev)
+
+    def parts(it):
+        g_ = torch.Generator().manual_seed(100 + it)
+        return [torch.randn(2048, generator=g_) for _ in range(world)], torch.randn(2048, generator=g_)
+
+    def want_sum(ps, r0):
+        a = r0.clone()
+        for q in range(world):
+            a = a + ps[q]
+        return a
+
+    for it in range(2):
+        ps, r0 = parts(it)
+        red_part.copy_(ps[rank].to(dev))
+        res.copy_(r0.to(dev))
+        pg.allreduce("r", red_part, res, red_out)
+        pg.gather("v", part)
+        torch.cuda.synchronize(dev)
+        ok &= bool(torch.equal(red_out.cpu(), want_sum(ps, r0)))
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        pg.allreduce("r", red_part, res, red_out)
+        pg.gather("w", part2)
+        pg.allreduce("r", red_out, res, red_out2)
+    for it in range(2, 5):
+        ps, r0 = parts(it)
+        red_part.copy_(ps[rank].to(dev))
+        res.copy_(r0.to(dev))
+        g2.replay()
+        torch.cuda.synchronize(dev)
+        first = want_sum(ps, r0)
+        # the second all-reduce sums every rank's first result (identical on all ranks)
+        ok &= bool(torch.equal(red_out.cpu(), first))
+        ok &= bool(torch.equal(red_out2.cpu(), want_sum([first] * world, r0)))
     ok &= not pg.timed_out()
+    del g2
     del g
     pg.close()
     with open(os.path.join(out_dir, f"gather{rank}"), "w") as f:

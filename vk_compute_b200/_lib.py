@@ -38,6 +38,7 @@ SIGNATURES = {
     "vkc_quantize": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p]),
     "vkc_pack_block16": (_i, [_p, _p, _i, _i, _i, _p]),
     "vkc_allgather_p2p": (_i, [_p, _p, _p, _i, _i, _i, _p, _p]),
+    "vkc_allreduce_residual_p2p": (_i, [_p, _p, _p, _i, _i, _i, _p, _p, _p, _p]),
     "vkc_ipc_alloc": (_i, [_sz, C.POINTER(C.c_void_p), _p]),
     "vkc_ipc_open": (_i, [_p, C.POINTER(C.c_void_p)]),
     "vkc_ipc_close": (_i, [_p]),

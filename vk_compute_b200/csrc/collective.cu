@@ -85,6 +85,65 @@ __global__ void __launch_bounds__(kGatherThreads) allgather_kernel(const float4*
     __syncthreads();
 }
 
+// All-reduce with residual for K-split projections: every rank holds a
+// partial output vector (its K slice of the product); the slices are stored
+// into slot `rank` of every rank's partial buffer [world][n], the same
+// arrival protocol as above runs, and each rank then writes
+// out = residual + sum over ranks (in rank order, so every rank computes the
+// same bits) of the slots.
+__global__ void __launch_bounds__(kGatherThreads) allreduce_residual_kernel(
+    const float4* __restrict__ part, float* const* slots, unsigned* const* ctrs, int n4, int rank, int world,
+    const float4* __restrict__ residual, float4* __restrict__ out, unsigned* status) {
+    pdl_launch_dependents();
+    pdl_wait();  // the partial comes from the previous kernel
+    const int stride = gridDim.x * blockDim.x;
+    for (int p = 0; p < world; ++p) {
+        float4* d = reinterpret_cast<float4*>(slots[p]) + static_cast<size_t>(rank) * n4;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) d[i] = part[i];
+    }
+    __syncthreads();
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        unsigned target = 0;
+        for (int p = 0; p < world; ++p) {
+            if (p == rank) {
+                const unsigned old = atom_add_relaxed_sys(ctrs[p] + rank, 1u);
+                target = (old / gridDim.x + 1) * gridDim.x;
+            } else {
+                red_add_relaxed_sys(ctrs[p] + rank, 1u);
+            }
+        }
+        const unsigned* mine = ctrs[rank];
+        bool ok = true;
+        for (int q = 0; q < world && ok; ++q) {
+            uint32_t it = 0;
+            while (static_cast<int>(ld_relaxed_sys(mine + q) - target) < 0) {
+                if (++it > kSpinLimit) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        fence_acq_rel_sys();
+        if (!ok) atomicOr(status, kStatusPeerTimeout);
+        s_ok = ok;
+    }
+    __syncthreads();
+    const float4* mine4 = reinterpret_cast<const float4*>(slots[rank]);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 a = residual[i];
+        for (int q = 0; q < world; ++q) {
+            const float4 v = __ldcg(mine4 + static_cast<size_t>(q) * n4 + i);
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        out[i] = a;
+    }
+}
+
 }  // namespace
 }  // namespace vkc
 
@@ -108,6 +167,30 @@ int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* coun
     cfg.numAttrs = launch_attrs(attrs, 1);
     VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, allgather_kernel, reinterpret_cast<const float4*>(src),
                                     reinterpret_cast<float* const*>(dsts), counters, slice_floats / 4, rank, world,
+                                    status));
+    return kOk;
+}
+
+int vkc_allreduce_residual_p2p(const float* part, void* const* slots, unsigned* const* counters, int n, int rank,
+                               int world, const float* residual, float* out, unsigned* status, void* stream) {
+    if (!part || !slots || !counters || !residual || !out || !status)
+        return set_error(kErrArg, "null all-reduce pointer");
+    if (world < 1 || rank < 0 || rank >= world) return set_error(kErrArg, "rank %d of world %d", rank, world);
+    if (n <= 0 || n % 4 != 0) return set_error(kErrArg, "vector of %d floats (must be a positive multiple of 4)", n);
+    if ((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(residual) |
+         reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+        return set_error(kErrArg, "part, residual and out must be 16-byte aligned");
+    if (out == part) return set_error(kErrArg, "out must not alias part");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kGatherCtas, 1, 1);
+    cfg.blockDim = dim3(kGatherThreads, 1, 1);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[2];
+    cfg.attrs = attrs;
+    cfg.numAttrs = launch_attrs(attrs, 1);
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, allreduce_residual_kernel, reinterpret_cast<const float4*>(part),
+                                    reinterpret_cast<float* const*>(slots), counters, n / 4, rank, world,
+                                    reinterpret_cast<const float4*>(residual), reinterpret_cast<float4*>(out),
                                     status));
     return kOk;
 }

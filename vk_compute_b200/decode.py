@@ -15,12 +15,17 @@ ships these operators as separate shaders and no driver chains them
 RmsNorm-swiglu-ffn-*.comp); the chain, the KV append and the residual adds are
 this library's.
 
-Sharding over `world` GPUs of one node (one process each): rank r owns query
-heads [r*nq/world, (r+1)*nq/world) and the matching KV heads, so QKV,
-RoPE, the cache and attention are local; the O, gate/up and down projections
-are split by output rows.  Four all-gathers per layer assemble the attention
-output, x', h and x'' from the ranks' slices (NVLink peer stores by default,
-NCCL on request).
+Sharding over `world` GPUs of one node (one process each), two exchanges per
+layer: rank r owns query heads [r*nq/world, (r+1)*nq/world) and the matching
+KV heads, so QKV (split by output rows, head-aligned), RoPE, the cache and
+attention are local; the O projection is split along its input (the rank's
+heads), so each rank produces a partial x' increment; gate/up are split by
+output rows (the rank's slice of h) and down along its input (that slice).
+The two partial vectors per layer are summed across ranks together with the
+residual by an all-reduce (the library's NVLink peer all-reduce by default,
+NCCL on request), leaving x' and x'' replicated on every rank.  Splitting O
+and down along K keeps their quantisation identical to the unsharded matrices
+(scales are per input row and 256-output block).
 """
 from __future__ import annotations
 
@@ -60,8 +65,8 @@ class ShardPlan:
     q_heads: tuple[int, int]     # [lo, hi) query heads
     kv_heads: tuple[int, int]    # [lo, hi) KV heads
     qkv_cols: tuple[int, ...]    # output rows of the full QKV matrix, shard order [Q | K | V]
-    o_rows: tuple[int, int]      # [lo, hi) of hidden
-    ffn_rows: tuple[int, int]    # [lo, hi) of inter
+    o_k: tuple[int, int]         # [lo, hi) of the O projection's input (the rank's heads x head_dim)
+    ffn_rows: tuple[int, int]    # [lo, hi) of inter: gate/up outputs, down inputs
 
     @property
     def n_q(self) -> int:
@@ -87,14 +92,17 @@ def shard_plan(cfg: DecoderConfig, rank: int, world: int) -> ShardPlan:
     q_cols = range(q0 * hd, (q0 + nq) * hd)
     k_cols = range(cfg.n_q * hd + k0 * hd, cfg.n_q * hd + (k0 + nkv) * hd)
     v_cols = range((cfg.n_q + cfg.n_kv) * hd + k0 * hd, (cfg.n_q + cfg.n_kv) * hd + (k0 + nkv) * hd)
-    h = cfg.hidden // world
     f = cfg.inter // world
     plan = ShardPlan(rank, world, (q0, q0 + nq), (k0, k0 + nkv), tuple(q_cols) + tuple(k_cols) + tuple(v_cols),
-                     (rank * h, (rank + 1) * h), (rank * f, (rank + 1) * f))
+                     (q0 * hd, (q0 + nq) * hd), (rank * f, (rank + 1) * f))
     if cfg.bits <= 8:
-        for n in (len(plan.qkv_cols), h, f):
+        for n in (len(plan.qkv_cols), f):
             if n % 256:
                 raise ValueError(f"a {cfg.bits}-bit shard of {n} rows is not a whole number of 256-row scale blocks")
+    kpc = 128 // cfg.bits
+    for k in (nq * hd, f):
+        if k % kpc:
+            raise ValueError(f"an input slice of {k} is not a whole number of {kpc}-row chunks")
     return plan
 
 
@@ -128,18 +136,21 @@ def _pack(w: torch.Tensor, bits: int) -> ops.PackedWeight:
 
 def build_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: int = 0) -> LayerShard:
     """Random-init weights of one layer, this rank's shard.  Every rank draws
-    the same full matrices from the same seeds and keeps its own rows, so the
-    sharded model equals the unsharded one."""
+    the same full matrices from the same seeds and keeps its own part (QKV
+    and gate/up: output rows; O and down: input rows), so the sharded model
+    equals the unsharded one (for int4/int8, up to the QKV shard's scale
+    blocks: its head-permuted rows group into other 256-row blocks)."""
     base = seed * 1000 + layer * 10
     H, I = cfg.hidden, cfg.inter
     cols = torch.tensor(plan.qkv_cols, device=device)
     qkv = _pack(dense_weight(base + 1, H, cfg.qkv_rows, cfg.w_std, device)[:, cols].contiguous(), cfg.bits)
-    o_lo, o_hi = plan.o_rows
+    ok_lo, ok_hi = plan.o_k
     f_lo, f_hi = plan.ffn_rows
-    o = _pack(dense_weight(base + 2, H, H, cfg.w_std, device)[:, o_lo:o_hi].contiguous(), cfg.bits)
+    o = _pack(dense_weight(base + 2, cfg.n_q * cfg.head_dim, H, cfg.w_std, device)[ok_lo:ok_hi].contiguous(),
+              cfg.bits)
     gate = _pack(dense_weight(base + 3, H, I, cfg.w_std, device)[:, f_lo:f_hi].contiguous(), cfg.bits)
     up = _pack(dense_weight(base + 4, H, I, cfg.w_std, device)[:, f_lo:f_hi].contiguous(), cfg.bits)
-    down = _pack(dense_weight(base + 5, I, H, cfg.w_std, device)[:, o_lo:o_hi].contiguous(), cfg.bits)
+    down = _pack(dense_weight(base + 5, I, H, cfg.w_std, device)[f_lo:f_hi].contiguous(), cfg.bits)
     g = torch.Generator(device=device).manual_seed(base + 6)
     g_attn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
     g_ffn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
@@ -154,15 +165,13 @@ def build_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: i
 
 @dataclass
 class Buffers:
-    x: torch.Tensor           # hidden state, full
-    x_mid: torch.Tensor       # x' (after attention block), full
+    x: torch.Tensor           # hidden state (replicated on every rank)
+    x_mid: torch.Tensor       # x' after the attention block (replicated)
     qkv: torch.Tensor         # this rank's QKV rows
-    attn: torch.Tensor        # this rank's attention output
-    attn_full: torch.Tensor
-    o_slice: torch.Tensor
-    h: torch.Tensor
-    h_full: torch.Tensor
-    d_slice: torch.Tensor
+    attn: torch.Tensor        # this rank's attention output (its heads)
+    h: torch.Tensor           # this rank's slice of the SwiGLU output
+    o_part: torch.Tensor      # this rank's partial O output (world > 1)
+    d_part: torch.Tensor      # this rank's partial down output (world > 1)
     ws: torch.Tensor          # attention workspace
 
 
@@ -171,11 +180,11 @@ class ShardedDecoder:
 
     `step(pos)` advances the hidden state `buf.x` by one token at position
     `pos` (attending to tokens [0, pos]) and returns it.  With world > 1 the
-    four all-gathers per layer run on the current stream either as the
-    library's NVLink peer all-gather (exchange="p2p", the default: the full
-    buffers live in peer-mapped memory, see p2p.PeerGather) or through
-    torch.distributed (exchange="nccl"); either way a step can be captured in a
-    CUDA graph.  Call close() before the process group is destroyed.
+    two all-reduces per layer run on the current stream either as the
+    library's NVLink peer all-reduce (exchange="p2p", the default: partial
+    slots live in peer-mapped memory, see p2p.PeerGather) or through
+    torch.distributed (exchange="nccl"); either way a step can be captured in
+    a CUDA graph.  Call close() before the process group is destroyed.
     """
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
@@ -190,22 +199,17 @@ class ShardedDecoder:
         self.layers = layers if layers is not None else [
             build_layer(cfg, self.plan, i, self.device, seed) for i in range(cfg.layers)]
         self.theta = rope_theta(cfg, self.device)
-        H, I, hd = cfg.hidden, cfg.inter, cfg.head_dim
+        H, hd = cfg.hidden, cfg.head_dim
         p = self.plan
         z = lambda n: torch.zeros(n, dtype=torch.float32, device=self.device)
         self.peer = None
-        full = {"x": H, "x_mid": H, "attn_full": cfg.n_q * hd, "h_full": I}
         if self.exchange == "p2p":
             from .p2p import PeerGather
 
-            self.peer = PeerGather(full, self.device, group)
-            fb = self.peer.buffers
-        else:
-            fb = {n: z(k) for n, k in full.items()}
+            self.peer = PeerGather({"o": world * H, "d": world * H}, self.device, group)
         self.buf = Buffers(
-            x=fb["x"], x_mid=fb["x_mid"], qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd), attn_full=fb["attn_full"],
-            o_slice=z(p.o_rows[1] - p.o_rows[0]), h=z(p.ffn_rows[1] - p.ffn_rows[0]), h_full=fb["h_full"],
-            d_slice=z(p.o_rows[1] - p.o_rows[0]),
+            x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd),
+            h=z(p.ffn_rows[1] - p.ffn_rows[0]), o_part=z(H), d_part=z(H),
             ws=ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device))
 
     # -- bytes one step streams on this rank (weights, scales, KV cache, at ctx)
@@ -217,17 +221,15 @@ class ShardedDecoder:
         kv = 2 * (pos + 1) * p.n_kv * cfg.head_dim * 2
         return n + cfg.layers * kv
 
-    def _gather(self, name: str, part: torch.Tensor) -> None:
-        out = getattr(self.buf, name)
-        if self.exchange == "none":
-            if out.data_ptr() != part.data_ptr():
-                out.copy_(part)
-        elif self.exchange == "p2p":
-            self.peer.gather(name, part)
+    def _reduce(self, slots: str, part: torch.Tensor, residual: torch.Tensor, out: torch.Tensor) -> None:
+        """out = residual + the sum over ranks of `part`."""
+        if self.exchange == "p2p":
+            self.peer.allreduce(slots, part, residual, out)
         else:
             import torch.distributed as dist
 
-            dist.all_gather_into_tensor(out, part, group=self.group)
+            dist.all_reduce(part, group=self.group)
+            torch.add(residual, part, out=out)
 
     def close(self) -> None:
         """Releases the peer-mapped buffers (collective over the group)."""
@@ -241,26 +243,26 @@ class ShardedDecoder:
             raise ValueError(f"position {pos} outside the cache of {cfg.ctx} tokens")
         hd = cfg.head_dim
         q_rows, kv_rows = p.n_q * hd, p.n_kv * hd
-        o0, o1 = p.o_rows
         scale = 1.0 / math.sqrt(hd)
         single = p.world == 1
         for L in self.layers:
             ops.qkv_rope_append(L.qkv, b.x, L.g_attn, self.theta, pos, head_dim=hd, q_rows=q_rows, kv_rows=kv_rows,
                                 kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv)
             ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
-                                 workspace=b.ws, out=b.attn_full if single else b.attn, ctx_cap=cfg.ctx)
-            if not single:
-                self._gather("attn_full", b.attn)
-            ops.gemv_residual(L.o, b.attn_full, b.x[o0:o1], out=b.x_mid if single else b.o_slice)
-            if not single:
-                self._gather("x_mid", b.o_slice)
-            ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h_full if single else b.h)
-            if not single:
-                self._gather("h_full", b.h)
-            ops.gemv_residual(L.down, b.h_full, b.x_mid[o0:o1], out=b.x if single else b.d_slice)
-            if not single:
-                self._gather("x", b.d_slice)
+                                 workspace=b.ws, out=b.attn, ctx_cap=cfg.ctx)
+            if single:
+                ops.gemv_residual(L.o, b.attn, b.x, out=b.x_mid)
+            else:
+                ops.gemv(L.o, b.attn, out=b.o_part)
+                self._reduce("o", b.o_part, b.x, b.x_mid)
+            ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h)
+            if single:
+                ops.gemv_residual(L.down, b.h, b.x_mid, out=b.x)
+            else:
+                ops.gemv(L.down, b.h, out=b.d_part)
+                self._reduce("d", b.d_part, b.x_mid, b.x)
         return b.x
 
     def kernels_per_step(self) -> int:
-        return (9 if self.exchange == "p2p" else 5) * self.cfg.layers
+        """Launches of this library per step (collective-library kernels excluded)."""
+        return (7 if self.exchange == "p2p" else 5) * self.cfg.layers

@@ -1,4 +1,4 @@
-"""NVLink peer all-gather for the row-sharded decoder chain.
+"""NVLink peer all-gather and all-reduce for the sharded decoder chain.
 
 `PeerGather` allocates, on every rank of a torch.distributed group (one GPU
 per rank, one node), one device region holding named fp32 "full" buffers and
@@ -8,7 +8,9 @@ part)` then runs the library's all-gather kernel: this rank's slice is stored
 directly into every rank's copy of the buffer, and the kernel returns on the
 GPU once all slices have arrived (bounded wait; see vkc_allgather_p2p).  No
 collective library is on the data path, so a gather is one small kernel launch
-that can be captured in a CUDA graph.
+that can be captured in a CUDA graph.  `allreduce(name, part, residual, out)`
+stores `part` into this rank's slot of every rank's buffer [world][n] and
+writes out = residual + the slots summed in rank order.
 """
 from __future__ import annotations
 
@@ -78,6 +80,19 @@ class PeerGather:
         check(lib().vkc_allgather_p2p(part.data_ptr(), self.dsts[name].data_ptr(), self.ctr_ptrs.data_ptr(), n,
                                       self.rank, self.world, self.status.data_ptr(), st))
         return full
+
+    def allreduce(self, name: str, part: torch.Tensor, residual: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out = residual + sum over ranks of `part`; buffers[name] holds the
+        world partial slots ([world][n])."""
+        slots = self.buffers[name]
+        n = part.numel()
+        if slots.numel() != n * self.world or residual.numel() != n or out.numel() != n:
+            raise ValueError(f"{name}: vector of {n} for {slots.numel()} slot floats over {self.world} ranks")
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().vkc_allreduce_residual_p2p(part.data_ptr(), self.dsts[name].data_ptr(), self.ctr_ptrs.data_ptr(),
+                                               n, self.rank, self.world, residual.data_ptr(), out.data_ptr(),
+                                               self.status.data_ptr(), st))
+        return out
 
     def timed_out(self) -> bool:
         """True if a wait of any gather so far ran out (reads the device)."""
