@@ -103,6 +103,52 @@ int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* z
                        const float* su, const float* zu, const float* x, const float* gamma,
                        float* h, int N, int K, float eps, int rms_dim, void* stream);
 
+/* ---- Fused NVLink exchange for the sharded decoder (no counterpart in the
+ * reference, which runs on one GPU).  A K-split projection (O, down) stores
+ * its partial output straight into every rank's slot buffer; the next
+ * operator sums the slots while loading its input.  Slot buffers hold 8-byte
+ * words (flag << 32 | fp32 bits), written and read whole, so no fence or
+ * counter orders data and arrival: a reader waits until a peer's word carries
+ * the flag that its own rank's word for the same element carries.  Buffers
+ * are peer-mapped memory (vkc_ipc_*), zeroed before the first exchange; every
+ * rank makes the same sequence of launches on buffers of the same shapes.  A
+ * buffer is written again only after an exchange on another buffer that
+ * every rank's consumer of this one precedes (the decoder alternates two
+ * buffers), so no rank overwrites slots a slower rank is still reading. */
+
+/* Input of a fused consumer: x = base + the `world` partial vectors of
+ * `slots` ([world][K] words in this rank's memory, 8-byte aligned) summed in
+ * rank order; the previous launch on the stream must be this rank's
+ * vkc_gemv_peer into the same buffer.  x is also stored to `save` (K floats)
+ * unless NULL.  A thread that has waited 100 ms in total sets bit 8 of the
+ * device status word (vkc_device_status) and stops waiting. */
+typedef struct vkc_peer_input {
+    const void* slots;
+    float* save;
+    int rank;
+    int world;
+} vkc_peer_input;
+
+/* y_partial = W^T x (this rank's K slice of the projection), stored at
+ * elements [rank*N, (rank+1)*N) of every rank's [world][N] word buffer
+ * (slots: device array of `world` pointers), each word carrying the flag of
+ * this rank's own copy of the element plus one. */
+int vkc_gemv_peer(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                  void* const* slots, int rank, int world, int N, int K, void* stream);
+
+/* vkc_rmsnorm_gemv_rope_kv and vkc_rmsnorm_swiglu with their input taken
+ * from a peer exchange (`x_base` + the slots of `in`; host pointer, read at
+ * the call). */
+int vkc_rmsnorm_gemv_rope_kv_peer(int bits, const void* w, const float* scale, const float* zero,
+                                  const float* x_base, const vkc_peer_input* in, const float* gamma,
+                                  const float* theta, float* y, int N, int K, float eps, int rms_dim,
+                                  int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
+                                  void* vcache, int ctx_cap, void* stream);
+int vkc_rmsnorm_swiglu_peer(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
+                            const float* su, const float* zu, const float* x_base,
+                            const vkc_peer_input* in, const float* gamma, float* h, int N, int K,
+                            float eps, int rms_dim, void* stream);
+
 /* Decode attention for one token.  Replaces shader/Att-full-FP16.comp.
  * q: [n_q][head_dim], fp16 (q_bits 16) or fp32 (q_bits 32);
  * kcache: fp16 K[t][kv][d] at (t*n_kv + kv)*head_dim + d;

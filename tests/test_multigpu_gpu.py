@@ -138,11 +138,26 @@ def _decode_child(rank, world, port, out_dir, exchange):
     x0 = torch.Generator().manual_seed(9)
     dec.buf.x.copy_(torch.randn(cfg.hidden, generator=x0).to(dev))
     torch.cuda.synchronize(dev)
-    for pos in range(3):
+    for pos in range(2):
         out = dec.step(pos)
+    # the third step from a CUDA graph (the fused exchange's counters keep growing)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
     torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    x_in = dec.buf.x.clone()
+    with torch.cuda.graph(g, stream=s):
+        dec.step(2)
+    dec.buf.x.copy_(x_in)  # capture does not run the step
+    g.replay()
+    torch.cuda.synchronize(dev)
+    out = dec.buf.x
+    timed_out = dec.timed_out()
     if rank == 0:
         np.save(os.path.join(out_dir, f"dec_{exchange}.npy"), out.cpu().numpy())
+    with open(os.path.join(out_dir, f"dec_{exchange}_{rank}.status"), "w") as f:
+        f.write("timeout" if timed_out else "ok")
+    del g
     dec.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -170,13 +185,15 @@ def test_p2p_allgather_two_gpus():
 
 
 @needs2
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+@pytest.mark.parametrize("exchange", ["p2p", "p2p-kernel", "nccl"])
 def test_sharded_decoder_matches_one_gpu(exchange):
     from vk_compute_b200.decode import DecoderConfig, ShardedDecoder
 
     with tempfile.TemporaryDirectory() as d:
         _run(_decode_child, 2, d, exchange)
         got = np.load(os.path.join(d, f"dec_{exchange}.npy"))
+        for r in range(2):
+            assert open(os.path.join(d, f"dec_{exchange}_{r}.status")).read() == "ok"
     cfg = DecoderConfig(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64, bits=16)
     dec = ShardedDecoder(cfg, seed=5, device="cuda:0")
     x0 = torch.Generator().manual_seed(9)

@@ -8,12 +8,12 @@
 // multicast objects).  A launch copies this rank's slice into every rank's
 // buffer at offset rank * slice; after a CTA barrier one thread makes the
 // stores visible system-wide with a single fence, adds one to this rank's
-// counter slot on every rank (relaxed, system scope), and waits (relaxed
-// polling, bounded, then a fence) until every rank's slot in this rank's
-// counters has reached this launch's target.  One fence per launch instead of
-// one per thread or per atomic: measured 6-7 us per gather on two B200s in a
-// CUDA graph, against 16-18 us with release atomics and per-thread fences and
-// 21-23 us for NCCL's all-gather.  Counters only grow: with a fixed number of
+// counter slot on every rank (relaxed, system scope), and waits (polling with
+// system-scope acquire loads, bounded) until every rank's slot in this rank's
+// counters has reached this launch's target.  One fence per
+// launch instead of one per thread or per atomic: measured 6-7 us per gather
+// on two B200s in a CUDA graph, against 16-18 us with release atomics and
+// per-thread fences and 21-23 us for NCCL's all-gather.  Counters only grow: with a fixed number of
 // CTAs per launch, the k-th launch of a rank targets k * kGatherCtas, which
 // each CTA derives from the value its own increment of its own slot returned,
 // so captured graphs can be replayed without resetting anything.  All ranks
@@ -28,22 +28,6 @@ namespace {
 
 constexpr int kGatherCtas = 1;
 constexpr int kGatherThreads = 512;
-constexpr unsigned kStatusPeerTimeout = 8u;
-
-__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ unsigned atom_add_relaxed_sys(unsigned* p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.add.relaxed.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-__device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
-    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kGatherThreads) allgather_kernel(const float4* __restrict__ src,
                                                                    float* const* dsts, unsigned* const* ctrs,
@@ -72,14 +56,14 @@ __global__ void __launch_bounds__(kGatherThreads) allgather_kernel(const float4*
         bool ok = true;
         for (int q = 0; q < world && ok; ++q) {
             uint32_t it = 0;
-            while (static_cast<int>(ld_relaxed_sys(mine + q) - target) < 0) {
+            // acquire: the peers' slices are read after their arrivals
+            while (static_cast<int>(ld_acquire_sys(mine + q) - target) < 0) {
                 if (++it > kSpinLimit) {
                     ok = false;
                     break;
                 }
             }
         }
-        fence_acq_rel_sys();  // acquire: the peers' slices after their arrivals
         if (!ok) atomicOr(status, kStatusPeerTimeout);
     }
     __syncthreads();
@@ -118,14 +102,13 @@ __global__ void __launch_bounds__(kGatherThreads) allreduce_residual_kernel(
         bool ok = true;
         for (int q = 0; q < world && ok; ++q) {
             uint32_t it = 0;
-            while (static_cast<int>(ld_relaxed_sys(mine + q) - target) < 0) {
+            while (static_cast<int>(ld_acquire_sys(mine + q) - target) < 0) {
                 if (++it > kSpinLimit) {
                     ok = false;
                     break;
                 }
             }
         }
-        fence_acq_rel_sys();
         if (!ok) atomicOr(status, kStatusPeerTimeout);
         s_ok = ok;
     }

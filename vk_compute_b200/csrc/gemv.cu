@@ -34,6 +34,7 @@
 // pairs of weights use the packed f32x2 add and FMA.  inv_rms and c_b are
 // scalars applied in the epilogue, after the cluster reduction.
 #include "vkc_common.cuh"
+#include "vk_compute_b200.h"
 
 #include <cuda_fp16.h>
 
@@ -87,6 +88,18 @@ struct GemvParams {
     uint16_t* kcache;
     uint16_t* vcache;
     int q_rows, kv_rows, ctx_cap;
+    // Peer output (plain GEMV, K-split shard): output j goes, as the 8-byte
+    // word (flag << 32 | float bits), to element prank*N + j of every rank's
+    // [pworld][N] word buffer (peer_slots: device array of pworld pointers),
+    // flag = the flag this rank's own copy of the element held + 1.
+    unsigned long long* const* peer_slots;
+    // Peer input: x = x (the base) + the pworld slots of xslots ([pworld][K]
+    // words, summed in rank order); each thread waits until a peer's element
+    // carries the flag its own slot's element has (written by this rank's
+    // producer, the previous kernel).  The first column block stores x in xsave.
+    const unsigned long long* xslots;
+    float* xsave;
+    int prank, pworld;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -215,7 +228,14 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
         if (p.residual && active && j < p.N) out += p.residual[j];
     }
     if (active && j < p.N) {
-        p.y[j] = out;
+        if (MODE == kGemv && p.peer_slots) {
+            const size_t e = static_cast<size_t>(p.prank) * p.N + j;
+            const unsigned flag = static_cast<unsigned>(__ldcg(p.peer_slots[p.prank] + e) >> 32) + 1u;
+            const unsigned long long word = (static_cast<unsigned long long>(flag) << 32) | __float_as_uint(out);
+            for (int q = 0; q < p.pworld; ++q) st_relaxed_sys_u64(p.peer_slots[q] + e, word);
+        } else {
+            p.y[j] = out;
+        }
         if constexpr (MODE == kRopePairs) {
             if (p.kcache && j >= p.q_rows) {
                 const int jj = j - p.q_rows;
@@ -295,11 +315,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
             }
         }
     };
+    bool gave_up = false;  // a peer wait ran out (100 ms): later elements do not wait again
     auto load_x = [&](int base) {
 #pragma unroll
         for (int q = 0; q < kMaxAct; ++q) {
             const int e = base + tid + q * kThreads;
-            av_x[q] = e < nk ? p.x[r0 * KPC + e] : 0.f;
+            float v = e < nk ? p.x[r0 * KPC + e] : 0.f;
+            if (p.xslots && e < nk) {
+                const int k = r0 * KPC + e;
+                const unsigned flag = static_cast<unsigned>(__ldcg(p.xslots + static_cast<size_t>(p.prank) * p.K + k) >> 32);
+                for (int w = 0; w < p.pworld; ++w) {
+                    const unsigned long long* src = p.xslots + static_cast<size_t>(w) * p.K + k;
+                    unsigned long long word = ld_relaxed_sys_u64(src);
+                    if (static_cast<unsigned>(word >> 32) != flag && !gave_up) {
+                        const uint64_t t0 = globaltimer_ns();
+                        while (static_cast<unsigned>((word = ld_relaxed_sys_u64(src)) >> 32) != flag) {
+                            if (globaltimer_ns() - t0 > kPeerWaitNs) {  // bounded: give up, flag it
+                                atomicOr(&g_status, kStatusPeerTimeout);
+                                gave_up = true;
+                                break;
+                            }
+                        }
+                    }
+                    v += __uint_as_float(static_cast<unsigned>(word));
+                }
+                if (p.xsave && blockIdx.y == 0) p.xsave[k] = v;
+            }
+            av_x[q] = v;
         }
     };
     float ss = 0.f, cz[NS];
@@ -589,10 +631,42 @@ int vkc_gemv_residual(int bits, const void* w, const float* scale, const float* 
     return launch_mode<kGemv>(bits, p, static_cast<cudaStream_t>(stream));
 }
 
-int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero, const float* x,
-                             const float* gamma, const float* theta, float* y, int N, int K, float eps,
-                             int rms_dim, int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
-                             void* vcache, int ctx_cap, void* stream) {
+int vkc_gemv_peer(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                  void* const* slots, int rank, int world, int N, int K, void* stream) {
+    if (!slots) return set_error(kErrArg, "null peer slots");
+    if (world < 1 || rank < 0 || rank >= world) return set_error(kErrArg, "rank %d of world %d", rank, world);
+    float dummy = 0.f;  // y is unused: check_common only wants a non-null output
+    if (int e = check_common(bits, N, K, w, scale, zero, x, &dummy, nullptr)) return e;
+    GemvParams p = {};
+    p.w[0] = static_cast<const uint8_t*>(w);
+    p.s[0] = scale;
+    p.z[0] = zero;
+    p.x = x;
+    p.N = N;
+    p.K = K;
+    p.peer_slots = reinterpret_cast<unsigned long long* const*>(slots);
+    p.prank = rank;
+    p.pworld = world;
+    return launch_mode<kGemv>(bits, p, static_cast<cudaStream_t>(stream));
+}
+
+static int set_peer_input(GemvParams& p, const vkc_peer_input* in) {
+    if (!in) return kOk;
+    if (!in->slots) return set_error(kErrArg, "null peer-input slots");
+    if (reinterpret_cast<uintptr_t>(in->slots) % 8 != 0) return set_error(kErrArg, "peer-input slots must be 8-byte aligned");
+    if (in->world < 1 || in->rank < 0 || in->rank >= in->world)
+        return set_error(kErrArg, "peer input: rank %d of world %d", in->rank, in->world);
+    p.xslots = static_cast<const unsigned long long*>(in->slots);
+    p.xsave = in->save;
+    p.prank = in->rank;
+    p.pworld = in->world;
+    return kOk;
+}
+
+static int rope_kv_impl(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                        const float* gamma, const float* theta, float* y, int N, int K, float eps, int rms_dim,
+                        int pos, int head_dim, int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
+                        void* stream, const vkc_peer_input* in) {
     if (!gamma || !theta || !kcache || !vcache) return set_error(kErrArg, "null gamma, theta or cache");
     if (int e = check_common(bits, N, K, w, scale, zero, x, y, gamma)) return e;
     if (rms_dim <= 0) return set_error(kErrArg, "rms_dim=%d must be positive", rms_dim);
@@ -622,7 +696,26 @@ int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const 
     p.q_rows = q_rows;
     p.kv_rows = kv_rows;
     p.ctx_cap = ctx_cap;
+    if (int e = set_peer_input(p, in)) return e;
     return launch_mode<kRopePairs>(bits, p, static_cast<cudaStream_t>(stream));
+}
+
+int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                             const float* gamma, const float* theta, float* y, int N, int K, float eps,
+                             int rms_dim, int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
+                             void* vcache, int ctx_cap, void* stream) {
+    return rope_kv_impl(bits, w, scale, zero, x, gamma, theta, y, N, K, eps, rms_dim, pos, head_dim, q_rows, kv_rows,
+                        kcache, vcache, ctx_cap, stream, nullptr);
+}
+
+int vkc_rmsnorm_gemv_rope_kv_peer(int bits, const void* w, const float* scale, const float* zero,
+                                  const float* x_base, const vkc_peer_input* in, const float* gamma,
+                                  const float* theta, float* y, int N, int K, float eps, int rms_dim, int pos,
+                                  int head_dim, int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
+                                  void* stream) {
+    if (!in) return set_error(kErrArg, "null peer input");
+    return rope_kv_impl(bits, w, scale, zero, x_base, gamma, theta, y, N, K, eps, rms_dim, pos, head_dim, q_rows,
+                        kv_rows, kcache, vcache, ctx_cap, stream, in);
 }
 
 int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* zero, const float* x,
@@ -675,9 +768,9 @@ int vkc_rmsnorm_gemv_rope(int bits, const void* w, const float* scale, const flo
     return launch_mode<kRopePairs>(bits, p, s);
 }
 
-int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
-                       const float* su, const float* zu, const float* x, const float* gamma, float* h, int N,
-                       int K, float eps, int rms_dim, void* stream) {
+static int swiglu_impl(int bits, const void* wg, const float* sg, const float* zg, const void* wu, const float* su,
+                       const float* zu, const float* x, const float* gamma, float* h, int N, int K, float eps,
+                       int rms_dim, void* stream, const vkc_peer_input* in) {
     if (!gamma) return set_error(kErrArg, "null gamma");
     if (int e = check_common(bits, N, K, wg, sg, zg, x, h, gamma)) return e;
     if (int e = check_common(bits, N, K, wu, su, zu, x, h, gamma)) return e;
@@ -696,7 +789,21 @@ int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* z
     p.K = K;
     p.eps = eps;
     p.inv_dim = 1.0f / static_cast<float>(rms_dim);
+    if (int e = set_peer_input(p, in)) return e;
     return launch_mode<kSwiglu>(bits, p, static_cast<cudaStream_t>(stream));
+}
+
+int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
+                       const float* su, const float* zu, const float* x, const float* gamma, float* h, int N,
+                       int K, float eps, int rms_dim, void* stream) {
+    return swiglu_impl(bits, wg, sg, zg, wu, su, zu, x, gamma, h, N, K, eps, rms_dim, stream, nullptr);
+}
+
+int vkc_rmsnorm_swiglu_peer(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
+                            const float* su, const float* zu, const float* x_base, const vkc_peer_input* in,
+                            const float* gamma, float* h, int N, int K, float eps, int rms_dim, void* stream) {
+    if (!in) return set_error(kErrArg, "null peer input");
+    return swiglu_impl(bits, wg, sg, zg, wu, su, zu, x_base, gamma, h, N, K, eps, rms_dim, stream, in);
 }
 
 // Status word of the current device (bits: kStatus*).  Reading waits for the

@@ -186,7 +186,52 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 
 // Status bits a kernel records when a bounded wait gives up (see
 // vkc_device_status).
-enum : uint32_t { kStatusProducerTimeout = 1u, kStatusConsumerTimeout = 2u, kStatusReduceTimeout = 4u };
+enum : uint32_t {
+    kStatusProducerTimeout = 1u,
+    kStatusConsumerTimeout = 2u,
+    kStatusReduceTimeout = 4u,
+    kStatusPeerTimeout = 8u,  // a wait on other GPUs' arrivals ran out
+};
+
+// System-scope (other GPUs) relaxed accesses and the fence that orders them:
+// the arrival counters of the NVLink peer exchanges.
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned atom_add_relaxed_sys(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.relaxed.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_add_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Longest a thread waits, in total, for other GPUs' data in a fused exchange.
+constexpr uint64_t kPeerWaitNs = 100ull * 1000 * 1000;
+
+// 8-byte words read and written whole (single-copy atomic), for exchanges
+// that carry a flag beside each value instead of ordering data and flags.
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 
 __device__ __forceinline__ float warp_sum(float v) {

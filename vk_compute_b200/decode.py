@@ -22,8 +22,14 @@ attention are local; the O projection is split along its input (the rank's
 heads), so each rank produces a partial x' increment; gate/up are split by
 output rows (the rank's slice of h) and down along its input (that slice).
 The two partial vectors per layer are summed across ranks together with the
-residual by an all-reduce (the library's NVLink peer all-reduce by default,
-NCCL on request), leaving x' and x'' replicated on every rank.  Splitting O
+residual, leaving x' and x'' replicated on every rank.  By default the sum is
+fused into the operators: the O and down projections store their partials
+straight into every rank's slot buffer over NVLink (vkc_gemv_peer), and the
+next operator (SwiGLU, or the next layer's QKV) adds the slots to the
+residual while loading its input and stores the result (exchange="p2p"; the
+last layer of a step ends with a standalone peer all-reduce so that x is
+materialised).  exchange="p2p-kernel" runs the peer all-reduce as its own
+kernel after each projection, exchange="nccl" uses torch.distributed.  Splitting O
 and down along K keeps their quantisation identical to the unsharded matrices
 (scales are per input row and 256-output block).
 """
@@ -180,12 +186,15 @@ class ShardedDecoder:
 
     `step(pos)` advances the hidden state `buf.x` by one token at position
     `pos` (attending to tokens [0, pos]) and returns it.  With world > 1 the
-    two all-reduces per layer run on the current stream either as the
-    library's NVLink peer all-reduce (exchange="p2p", the default: partial
-    slots live in peer-mapped memory, see p2p.PeerGather) or through
+    two all-reduces per layer run on the current stream: fused into the
+    projections and their consumers (exchange="p2p", the default), as the
+    library's peer all-reduce kernel (exchange="p2p-kernel"; both keep the
+    partial slots in peer-mapped memory, see p2p.PeerGather) or through
     torch.distributed (exchange="nccl"); either way a step can be captured in
     a CUDA graph.  Call close() before the process group is destroyed.
     """
+
+    EXCHANGES = ("p2p", "p2p-kernel", "nccl")
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
                  group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p"):
@@ -193,8 +202,8 @@ class ShardedDecoder:
         self.plan = shard_plan(cfg, rank, world)
         self.device = torch.device(device or "cuda")
         self.group = group
-        if exchange not in ("p2p", "nccl"):
-            raise ValueError(f"exchange {exchange!r} (expected 'p2p' or 'nccl')")
+        if exchange not in self.EXCHANGES:
+            raise ValueError(f"exchange {exchange!r} (expected one of {self.EXCHANGES})")
         self.exchange = exchange if world > 1 else "none"
         self.layers = layers if layers is not None else [
             build_layer(cfg, self.plan, i, self.device, seed) for i in range(cfg.layers)]
@@ -203,14 +212,22 @@ class ShardedDecoder:
         p = self.plan
         z = lambda n: torch.zeros(n, dtype=torch.float32, device=self.device)
         self.peer = None
-        if self.exchange == "p2p":
-            from .p2p import PeerGather
-
-            self.peer = PeerGather({"o": world * H, "d": world * H}, self.device, group)
         self.buf = Buffers(
             x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd),
             h=z(p.ffn_rows[1] - p.ffn_rows[0]), o_part=z(H), d_part=z(H),
             ws=ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device))
+        if self.exchange in ("p2p", "p2p-kernel"):
+            from .p2p import PeerGather
+
+            # float slots for the all-reduce kernel; flagged 8-byte words for
+            # the fused exchange (x' = x + o words, saved to x_mid; x = x' + d)
+            sizes = {"o": world * H, "d": world * H}
+            if self.exchange == "p2p":
+                sizes.update(o_ll=2 * world * H, d_ll=2 * world * H)
+            self.peer = PeerGather(sizes, self.device, group)
+            if self.exchange == "p2p":
+                self._in_o = self.peer.peer_input("o_ll", save=self.buf.x_mid)
+                self._in_d = self.peer.peer_input("d_ll", save=self.buf.x)
 
     # -- bytes one step streams on this rank (weights, scales, KV cache, at ctx)
     def step_bytes(self, pos: int) -> int:
@@ -223,7 +240,7 @@ class ShardedDecoder:
 
     def _reduce(self, slots: str, part: torch.Tensor, residual: torch.Tensor, out: torch.Tensor) -> None:
         """out = residual + the sum over ranks of `part`."""
-        if self.exchange == "p2p":
+        if self.exchange in ("p2p", "p2p-kernel"):
             self.peer.allreduce(slots, part, residual, out)
         else:
             import torch.distributed as dist
@@ -245,24 +262,44 @@ class ShardedDecoder:
         q_rows, kv_rows = p.n_q * hd, p.n_kv * hd
         scale = 1.0 / math.sqrt(hd)
         single = p.world == 1
-        for L in self.layers:
-            ops.qkv_rope_append(L.qkv, b.x, L.g_attn, self.theta, pos, head_dim=hd, q_rows=q_rows, kv_rows=kv_rows,
-                                kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv)
+        fused = self.exchange == "p2p"
+        last = len(self.layers) - 1
+        for li, L in enumerate(self.layers):
+            # x: the step's input, or x' + the previous layer's down slots
+            base, peer_in = (b.x_mid, self._in_d) if fused and li > 0 else (b.x, None)
+            ops.qkv_rope_append(L.qkv, base, L.g_attn, self.theta, pos, head_dim=hd, q_rows=q_rows, kv_rows=kv_rows,
+                                kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv,
+                                peer=peer_in)
             ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
                                  workspace=b.ws, out=b.attn, ctx_cap=cfg.ctx)
             if single:
                 ops.gemv_residual(L.o, b.attn, b.x, out=b.x_mid)
+                ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h)
+            elif fused:
+                ops.gemv_peer(L.o, b.attn, self.peer.dsts["o_ll"], p.rank, p.world)
+                ops.rmsnorm_swiglu(L.gate, L.up, b.x, L.g_ffn, eps=cfg.eps, out=b.h, peer=self._in_o)
             else:
                 ops.gemv(L.o, b.attn, out=b.o_part)
                 self._reduce("o", b.o_part, b.x, b.x_mid)
-            ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h)
+                ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h)
             if single:
                 ops.gemv_residual(L.down, b.h, b.x_mid, out=b.x)
+            elif fused and li < last:
+                ops.gemv_peer(L.down, b.h, self.peer.dsts["d_ll"], p.rank, p.world)
             else:
                 ops.gemv(L.down, b.h, out=b.d_part)
                 self._reduce("d", b.d_part, b.x_mid, b.x)
         return b.x
 
+    def timed_out(self) -> bool:
+        """True if a wait on another rank ran out in any step so far (reads
+        and clears the device status word; synchronises)."""
+        if self.peer is None:
+            return False
+        return self.peer.timed_out() or bool(ops.device_status(clear=True) & 8)
+
     def kernels_per_step(self) -> int:
         """Launches of this library per step (collective-library kernels excluded)."""
-        return (7 if self.exchange == "p2p" else 5) * self.cfg.layers
+        if self.exchange == "p2p":
+            return 5 * self.cfg.layers + 1
+        return (7 if self.exchange == "p2p-kernel" else 5) * self.cfg.layers

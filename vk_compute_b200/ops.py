@@ -139,14 +139,38 @@ def gemv_residual(w: PackedWeight, x: torch.Tensor, residual: torch.Tensor, out=
     return y
 
 
+class PeerInput(C.Structure):
+    """vkc_peer_input: x = base + the `world` slots of this rank's [world][K]
+    word buffer (flag << 32 | fp32 bits, filled by the ranks' gemv_peer),
+    each element read once its flag matches this rank's own; x is also
+    stored to `save`."""
+
+    _fields_ = [("slots", C.c_void_p), ("save", C.c_void_p), ("rank", C.c_int), ("world", C.c_int)]
+
+
+def gemv_peer(w: PackedWeight, x: torch.Tensor, slots: torch.Tensor, rank: int, world: int, stream=None) -> None:
+    """This rank's K-split partial W^T x stored into slot `rank` of every
+    rank's word buffer (`slots`: int64 device tensor of the ranks' buffer
+    addresses), each value with its flag."""
+    check(lib().vkc_gemv_peer(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(slots), rank, world, w.N,
+                              w.K, _s(stream)))
+
+
 def qkv_rope_append(w: PackedWeight, x, gamma, theta, pos: int, *, head_dim: int, q_rows: int, kv_rows: int,
                     kcache: torch.Tensor, vcache: torch.Tensor, ctx_cap: int, eps: float = 1e-6,
-                    rms_dim: int | None = None, out=None, stream=None) -> torch.Tensor:
-    """Fused QKV projection + RoPE + KV-cache append at token `pos`."""
+                    rms_dim: int | None = None, out=None, stream=None, peer: PeerInput | None = None) -> torch.Tensor:
+    """Fused QKV projection + RoPE + KV-cache append at token `pos`; with
+    `peer`, the input is x (the base) plus the peer exchange's slots."""
     y = _out(w.N, x, out)
-    check(lib().vkc_rmsnorm_gemv_rope_kv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma), _p(theta),
-                                         _p(y), w.N, w.K, eps, rms_dim or w.K, pos, head_dim, q_rows, kv_rows,
-                                         _p(kcache), _p(vcache), ctx_cap, _s(stream)))
+    if peer is None:
+        check(lib().vkc_rmsnorm_gemv_rope_kv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma),
+                                             _p(theta), _p(y), w.N, w.K, eps, rms_dim or w.K, pos, head_dim, q_rows,
+                                             kv_rows, _p(kcache), _p(vcache), ctx_cap, _s(stream)))
+    else:
+        check(lib().vkc_rmsnorm_gemv_rope_kv_peer(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x),
+                                                  C.addressof(peer), _p(gamma), _p(theta), _p(y), w.N, w.K, eps,
+                                                  rms_dim or w.K, pos, head_dim, q_rows, kv_rows, _p(kcache),
+                                                  _p(vcache), ctx_cap, _s(stream)))
     return y
 
 
@@ -171,11 +195,18 @@ def rmsnorm_gemv_rope(w: PackedWeight, x, gamma, theta, pos: int, *, mode: str =
 
 
 def rmsnorm_swiglu(wg: PackedWeight, wu: PackedWeight, x, gamma, eps: float = 1e-6,
-                   rms_dim: int | None = None, out=None, stream=None) -> torch.Tensor:
+                   rms_dim: int | None = None, out=None, stream=None, peer: PeerInput | None = None) -> torch.Tensor:
+    """h = SiLU(Wg^T n) * (Wu^T n), n = RmsNorm(x) * gamma; with `peer`, the
+    input is x (the base) plus the peer exchange's slots."""
     h = _out(wg.N, x, out)
-    check(lib().vkc_rmsnorm_swiglu(wg.bits, _p(wg.packed), _p(wg.scale), _p(wg.zero), _p(wu.packed),
-                                   _p(wu.scale), _p(wu.zero), _p(x), _p(gamma), _p(h), wg.N, wg.K, eps,
-                                   rms_dim or wg.K, _s(stream)))
+    if peer is None:
+        check(lib().vkc_rmsnorm_swiglu(wg.bits, _p(wg.packed), _p(wg.scale), _p(wg.zero), _p(wu.packed),
+                                       _p(wu.scale), _p(wu.zero), _p(x), _p(gamma), _p(h), wg.N, wg.K, eps,
+                                       rms_dim or wg.K, _s(stream)))
+    else:
+        check(lib().vkc_rmsnorm_swiglu_peer(wg.bits, _p(wg.packed), _p(wg.scale), _p(wg.zero), _p(wu.packed),
+                                            _p(wu.scale), _p(wu.zero), _p(x), C.addressof(peer), _p(gamma), _p(h),
+                                            wg.N, wg.K, eps, rms_dim or wg.K, _s(stream)))
     return h
 
 
@@ -234,3 +265,11 @@ def gemm_bf16_status(clear: bool = True) -> int:
 
 def set_pdl(enable: bool) -> None:
     lib().vkc_set_pdl(int(enable))
+
+
+def device_status(clear: bool = False) -> int:
+    """Status word of the current device (waits for it): bit 1 producer, 2
+    consumer, 4 cluster reduction, 8 peer-exchange wait ran out."""
+    v = C.c_uint(0)
+    check(lib().vkc_device_status(C.byref(v), int(clear)))
+    return int(v.value)

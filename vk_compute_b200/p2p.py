@@ -94,6 +94,15 @@ class PeerGather:
                                                self.status.data_ptr(), st))
         return out
 
+    def peer_input(self, name: str, save: torch.Tensor | None = None):
+        """The fused-consumer descriptor of buffers[name] ([world][n] 8-byte
+        words, i.e. 2*world*n floats of the region, filled by ops.gemv_peer
+        with dsts[name])."""
+        from .ops import PeerInput
+
+        return PeerInput(self.buffers[name].data_ptr(), save.data_ptr() if save is not None else None, self.rank,
+                         self.world)
+
     def timed_out(self) -> bool:
         """True if a wait of any gather so far ran out (reads the device)."""
         return bool(int(self.status.item()) & 8)
