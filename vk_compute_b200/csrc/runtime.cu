@@ -127,11 +127,36 @@ struct Ctx {
     // Pinned staging for small writeBuffer uploads: the caller's bytes are
     // copied here, so the call can return before the device copy has run.
     void* stage[2];
-    cudaEvent_t staged[2];  // recorded after the last upload from each slot
+    bool stage_busy[2];  // an upload from the slot may still be in flight
     int next;
-    void* rstage;  // pinned landing buffer for small reads
+    void* rstage;  // mapped pinned landing buffer for small reads
+    void* rstage_dev;  // its device address
 };
 constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronously
+
+void stream_synced(Ctx* c) { c->stage_busy[0] = c->stage_busy[1] = false; }
+
+// Device -> mapped host copy for readBuffer: a kernel rather than a DMA copy
+// (lower latency for the kilobytes a decode step reads back).  Runs after the
+// previous kernel has completed (no early launch), so it sees its results.
+__global__ void download_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
+                                uint8_t* __restrict__ dst_tail, const uint8_t* __restrict__ src_tail, int tail) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
+    if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < tail) dst_tail[threadIdx.x] = src_tail[threadIdx.x];
+}
+
+cudaError_t launch_download(void* dst, const void* src, size_t n, cudaStream_t stream) {
+    const size_t n16 = n / 16;
+    const int tail = static_cast<int>(n % 16);
+    int blocks = static_cast<int>((n16 + 255) / 256);
+    if (blocks < 1) blocks = 1;
+    if (blocks > 148) blocks = 148;
+    download_kernel<<<blocks, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
+                                                 static_cast<uint8_t*>(dst) + n16 * 16,
+                                                 static_cast<const uint8_t*>(src) + n16 * 16, tail);
+    return cudaGetLastError();
+}
 constexpr uint32_t kCtxMagic = 0x564b4331u;  // "VKC1"
 
 [[noreturn]] void fatal(const char* fmt, ...) {
@@ -151,7 +176,9 @@ void check_cuda(cudaError_t e, const char* what) {
 Ctx* ctx_of(const void* handle) {
     Ctx* c = reinterpret_cast<Ctx*>(const_cast<void*>(handle));
     if (!c || c->magic != kCtxMagic) fatal("invalid device handle");
-    check_cuda(cudaSetDevice(c->ordinal), "cudaSetDevice");
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != c->ordinal)
+        check_cuda(cudaSetDevice(c->ordinal), "cudaSetDevice");
     return c;
 }
 
@@ -393,11 +420,12 @@ device createDevice() {
     check_cuda(cudaEventCreate(&c->ev_begin), "cudaEventCreate");
     check_cuda(cudaEventCreate(&c->ev_end), "cudaEventCreate");
     for (int i = 0; i < 2; ++i) {
-        check_cuda(cudaEventCreateWithFlags(&c->staged[i], cudaEventDisableTiming), "cudaEventCreate");
         c->stage[i] = nullptr;
+        c->stage_busy[i] = false;
     }
     c->next = 0;
     c->rstage = nullptr;
+    c->rstage_dev = nullptr;
     c->timed = false;
     device d;
     d.instance = reinterpret_cast<VkInstance>(c);
@@ -412,10 +440,8 @@ void destroyDevice(device dev) {
     cudaStreamSynchronize(c->stream);
     cudaEventDestroy(c->ev_begin);
     cudaEventDestroy(c->ev_end);
-    for (int i = 0; i < 2; ++i) {
-        cudaEventDestroy(c->staged[i]);
+    for (int i = 0; i < 2; ++i)
         if (c->stage[i]) cudaFreeHost(c->stage[i]);
-    }
     if (c->rstage) cudaFreeHost(c->rstage);
     cudaStreamDestroy(c->stream);
     c->magic = 0;
@@ -451,6 +477,7 @@ buffer createBuffer(VkDevice dev, VkPhysicalDevice, void* data, int64_t size, in
     else
         check_cuda(cudaMemsetAsync(p, 0, alloc ? alloc : 256, c->stream), "cudaMemsetAsync");
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    stream_synced(c);
     b.buffer = reinterpret_cast<VkBuffer>(p);
     b.memory = reinterpret_cast<VkDeviceMemory>(p);
     b.memReqs.size = alloc;
@@ -464,6 +491,7 @@ buffer createBuffer(VkDevice dev, VkPhysicalDevice, void* data, int64_t size, in
 void createTransferAndCopy(VkDevice dev, VkQueue, buffer*, int) {
     Ctx* c = ctx_of(dev);
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    stream_synced(c);
 }
 
 // Reads of up to kStageMax bytes land in a pinned staging buffer and are
@@ -474,15 +502,20 @@ void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* outpu
     if (!buf.buffer) fatal("readBuffer: empty buffer");
     const size_t n = static_cast<size_t>(buf.size);
     if (n > 0 && n <= kStageMax) {
-        if (!c->rstage) check_cuda(cudaHostAlloc(&c->rstage, kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
-        check_cuda(cudaMemcpyAsync(c->rstage, buf.buffer, n, cudaMemcpyDeviceToHost, c->stream), "cudaMemcpyAsync");
+        if (!c->rstage) {
+            check_cuda(cudaHostAlloc(&c->rstage, kStageMax, cudaHostAllocMapped), "cudaHostAlloc");
+            check_cuda(cudaHostGetDevicePointer(&c->rstage_dev, c->rstage, 0), "cudaHostGetDevicePointer");
+        }
+        check_cuda(launch_download(c->rstage_dev, buf.buffer, n, c->stream), "download kernel");
         check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+        stream_synced(c);
         memcpy(output, c->rstage, n);
         return;
     }
     if (n > 0)
         check_cuda(cudaMemcpyAsync(output, buf.buffer, n, cudaMemcpyDeviceToHost, c->stream), "cudaMemcpyAsync");
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    stream_synced(c);
 }
 
 // Uploads of up to kStageMax bytes go through the pinned staging buffer and
@@ -503,12 +536,16 @@ void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
     // before last has left it (normally long done).
     const int slot = c->next;
     c->next ^= 1;
-    if (cudaEventQuery(c->staged[slot]) != cudaSuccess)
-        check_cuda(cudaEventSynchronize(c->staged[slot]), "cudaEventSynchronize");
+    // A slot whose upload may still be in flight (no synchronisation of the
+    // stream since it was queued; every readBuffer synchronises) is waited for.
+    if (c->stage_busy[slot]) {
+        check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+        stream_synced(c);
+    }
     if (!c->stage[slot]) check_cuda(cudaHostAlloc(&c->stage[slot], kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
     memcpy(c->stage[slot], data, n);
     check_cuda(cudaMemcpyAsync(buf.buffer, c->stage[slot], n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
-    check_cuda(cudaEventRecord(c->staged[slot], c->stream), "cudaEventRecord");
+    c->stage_busy[slot] = true;
 }
 
 void destroyBuffer(VkDevice dev, buffer buf) {
