@@ -51,6 +51,8 @@ WORKLOADS = {
     "swiglu_ffn_int4": "RmsNorm-swiglu-ffn INT4 gate/up 12288x4096 + down GEMV INT4 4096x12288",
     "qkv_rope_attn_int4": "RmsNorm-GEMV-Rope INT4 QKV 6144x4096 (theta 1e6) + Att-full-FP16 32q/8kv x 128, ctx 8192",
     "prefill_gemm_bf16": "prefill GEMM bf16 on tcgen05: A 64x4096 . W^T (W 12288x4096, K-major) -> C 64x12288 fp32",
+    "rmsnorm_gemv_int8_batch4": "batched decode: RmsNorm-GEMV INT8 12288x4096 on 4 vectors (weights streamed once)",
+    "gemv_int4_batch8": "batched decode: GEMV INT4 4096x12288 (down projection) on 8 vectors (weights streamed once)",
 }
 
 
@@ -183,6 +185,27 @@ def build_workload(name: str, rank: int, device):
         return dict(step=step, bytes=wbytes + act, launches=1, dominant=step, dominant_bytes=wbytes + act,
                     dominant_name=("RmsNorm-GEMV-INT8" if bits == 8 else "GEMV-FP16"), meta=meta,
                     e2e=(pool, x, gamma, y, K, N, bits))
+
+    if name in ("rmsnorm_gemv_int8_batch4", "gemv_int4_batch8"):
+        if name == "rmsnorm_gemv_int8_batch4":
+            K, N, bits, M = 4096, 12288, 8, 4
+        else:
+            K, N, bits, M = 12288, 4096, 4, 8
+        x = randn(M, K)
+        gamma = randn(K, std=0.1, mean=1.0)
+        y = torch.empty(M, N, device=device)
+        wbytes = K * N * bits // 8 + 2 * 4 * K * N // 256
+        pool = pool_of(lambda j: ops.pack_dense(randn(K, N, std=0.02), bits, symmetric=True, fp16_scale=True),
+                       wbytes)
+        if bits == 8:
+            act = 4 * M * K + 4 * K + 4 * M * N
+            step = lambda i: ops.rmsnorm_gemv_batched(pool[i % len(pool)], x, gamma, eps=1e-6, out=y)
+        else:
+            act = 4 * M * K + 4 * M * N
+            step = lambda i: ops.gemv_batched(pool[i % len(pool)], x, out=y)
+        meta = {"K": K, "N": N, "bits": bits, "vectors": M, "pool": len(pool), "pool_bytes": len(pool) * wbytes}
+        return dict(step=step, bytes=wbytes + act, launches=1, dominant=step, dominant_bytes=wbytes + act,
+                    dominant_name=f"batched GEMV INT{bits} x{M}", meta=meta, e2e=None)
 
     if name == "swiglu_ffn_int4":
         H, I = 4096, 12288
@@ -432,12 +455,17 @@ def cpu_baseline(workload: str, budget_s: float = 12.0, threads: int | None = No
         return {"value": round(nbytes / per / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                 "sample": f"{reps} passes of 64x4096 . 4096x{Ns} (1/8 of the columns) in {el:.1f} s",
                 "s_per_pass": per}
+    vectors = 1
     if workload == "rmsnorm_gemv_int8":
         K, N, bits = 4096, 12288, 8
     elif workload == "gemv_fp16":
         K, N, bits = 4096, 4096, 16
     elif workload == "swiglu_ffn_int4":
         K, N, bits = 4096, 12288, 4
+    elif workload == "rmsnorm_gemv_int8_batch4":
+        K, N, bits, vectors = 4096, 12288, 8, 4
+    elif workload == "gemv_int4_batch8":
+        K, N, bits, vectors = 12288, 4096, 4, 8
     else:
         K, N, bits = 4096, 6144, 4
     w = (rng.standard_normal((K, N), dtype=np.float32) * 0.02)
@@ -449,7 +477,7 @@ def cpu_baseline(workload: str, budget_s: float = 12.0, threads: int | None = No
     else:
         data, s, z = o.quantize(w, bits, True, True)
         nbytes = K * N * bits // 8 + 8 * K * N // 256 + 8 * K + 4 * N
-    gamma = None if workload == "gemv_fp16" else g
+    gamma = None if workload in ("gemv_fp16", "gemv_int4_batch8") else g
     reps, t0 = 0, time.perf_counter()
     while True:
         if workload == "swiglu_ffn_int4":
@@ -462,8 +490,14 @@ def cpu_baseline(workload: str, budget_s: float = 12.0, threads: int | None = No
             break
     per = el / reps
     mult = 2 if workload == "swiglu_ffn_int4" else 1
+    if vectors > 1:
+        # the reference computes one vector per pass: a batch of M is M passes
+        # over the same bytes the batched kernel reads once
+        per *= vectors
+        nbytes = K * N * bits // 8 + 8 * K * N // 256 + vectors * 4 * (K + N)
     return {"value": round(mult * nbytes / per / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} full passes of {bits}-bit {K}x{N}{' gate+up' if mult == 2 else ''} in {el:.1f} s",
+            "sample": f"{reps} full passes of {bits}-bit {K}x{N}{' gate+up' if mult == 2 else ''} in {el:.1f} s"
+                      + (f", one vector per pass, {vectors} passes per step" if vectors > 1 else ""),
             "s_per_pass": per}
 
 

@@ -149,6 +149,17 @@ int vkc_rmsnorm_swiglu_peer(int bits, const void* wg, const float* sg, const flo
                             const vkc_peer_input* in, const float* gamma, float* h, int N, int K,
                             float eps, int rms_dim, void* stream);
 
+/* Batched decode (no counterpart in the reference: its shaders take an M push
+ * constant but compute one vector).  y[m] = W^T x[m] for M in 1..8 vectors
+ * (x: [M][K], y: [M][N], fp32, row-major) with the weights streamed once for
+ * all of them; the RmsNorm variant normalises each vector by its own RMS.
+ * M == 1 runs vkc_gemv / vkc_rmsnorm_gemv.  K must be a multiple of 4. */
+int vkc_gemv_batched(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                     float* y, int M, int N, int K, void* stream);
+int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const float* zero,
+                             const float* x, const float* gamma, float* y, int M, int N, int K,
+                             float eps, int rms_dim, void* stream);
+
 /* Decode attention for one token.  Replaces shader/Att-full-FP16.comp.
  * q: [n_q][head_dim], fp16 (q_bits 16) or fp32 (q_bits 32);
  * kcache: fp16 K[t][kv][d] at (t*n_kv + kv)*head_dim + d;

@@ -44,6 +44,8 @@ SIGNATURES = {
     "vkc_ipc_close": (_i, [_p]),
     "vkc_ipc_free": (_i, [_p]),
     "vkc_gemv_peer": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "vkc_gemv_batched": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _p]),
+    "vkc_rmsnorm_gemv_batched": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _f, _i, _p]),
     "vkc_rmsnorm_gemv_rope_kv_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p,
                                            _p, _i, _p]),
     "vkc_rmsnorm_swiglu_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),

@@ -493,6 +493,228 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
     }
 }
 
+// ---- Batched decode: M activation vectors against one weight stream -------
+// The same decomposition as gemv_kernel (cluster split K, per-thread cp.async
+// ring, rank-0 reduction over DSMEM), with M staged activation rows: each
+// weight chunk is decoded once into f32x2 pairs and multiplied into M
+// accumulators, so the weights stream from HBM once for all M vectors.
+constexpr int kMaxBatch = 8;
+
+struct BatchParams {
+    const uint8_t* w;
+    const float* s;
+    const float* z;
+    const float* x;      // [M][K]
+    const float* gamma;  // RmsNorm-GEMV; unused by the plain GEMV
+    float* y;            // [M][N]
+    int N, K, R;
+    int cols, rows_cta, rbuf_floats;
+    float eps, inv_dim;
+};
+
+// The KPC/2 weight pairs of one chunk, in the order of the staged activations
+// (pair p multiplies activations 2p and 2p+1): exact codes (minus the 2^23
+// bias) for int8/int4 -- int4 nibbles keep their bit position, the staged
+// activations carry the matching power of two -- and converted values for
+// fp16/fp32.
+template <int BITS>
+__device__ __forceinline__ void decode_pairs(const uint4 c, uint64_t (&w)[64 / BITS]) {
+    const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
+    if constexpr (BITS == 32) {
+        w[0] = f2_pack(__uint_as_float(c.x), __uint_as_float(c.y));
+        w[1] = f2_pack(__uint_as_float(c.z), __uint_as_float(c.w));
+    } else if constexpr (BITS == 16) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd[q]));
+            w[q] = f2_pack(f.x, f.y);
+        }
+    } else if constexpr (BITS == 8) {
+        const uint64_t neg = f2_pack(-8388608.0f, -8388608.0f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            w[2 * q] = f2_add(byte_pair<0x7540, 0x7541>(wd[q]), neg);
+            w[2 * q + 1] = f2_add(byte_pair<0x7542, 0x7543>(wd[q]), neg);
+        }
+    } else {
+        const uint64_t neg = f2_pack(-8388608.0f, -8388608.0f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t a = wd[q], h = a >> 12;
+            w[4 * q + 0] = f2_add(nib_pair(a, 0xFu, a, 0xF0u), neg);
+            w[4 * q + 1] = f2_add(nib_pair(a, 0xF00u, a, 0xF000u), neg);
+            w[4 * q + 2] = f2_add(nib_pair(a, 0xF0000u, h, 0xF00u), neg);
+            w[4 * q + 3] = f2_add(nib_pair(h, 0xF000u, h, 0xF0000u), neg);
+        }
+    }
+}
+
+template <int BITS, int M, bool NORM>
+__global__ void __launch_bounds__(kThreads, 2) gemv_batched_kernel(const BatchParams p) {
+    constexpr int KPC = 128 / BITS, NP = KPC / 2;
+    constexpr int D = 32768 / (kThreads * 16);  // rows in flight per thread
+    constexpr bool kQuant = BITS <= 8;
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* ring = reinterpret_cast<uint4*>(smem);                          // [D][256]
+    float* rbuf = reinterpret_cast<float*>(smem + D * kThreads * 16);      // [S][M*share + 2M]
+    float* xs = rbuf + p.rbuf_floats;                                      // [rows_cta][M][KPC]
+    __shared__ float red[M][kThreads];
+    __shared__ float wred[kThreads / 32][2 * M];
+    __shared__ __align__(8) uint64_t red_bar;
+
+    uint32_t nctarank, ctarank;
+    asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(nctarank));
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(ctarank));
+    const int S = static_cast<int>(nctarank);
+    const int rank = static_cast<int>(ctarank);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int C = p.cols, G = kThreads / C;
+    const int c = tid % C, grp = tid / C;
+    const int col0 = blockIdx.y * C;
+    const int col = col0 + c;
+    const bool col_ok = col < p.N;
+    const int r0 = rank * p.rows_cta;
+    const int nrows = max(0, min(p.rows_cta, p.R - r0));
+    const int nk = nrows * KPC;
+    const size_t sblk = static_cast<size_t>(col0 / kGroup) * p.K;
+
+    if (S > 1) {
+        if (tid == 0) {  // every rank receives the other S-1 ranks' deposits
+            mbar_init(smem_addr(&red_bar), static_cast<uint32_t>(S - 1));
+            mbar_init_fence();
+        }
+        cluster_arrive_release();
+    }
+    pdl_launch_dependents();
+
+    // weights never depend on the previous kernel: prime the ring first
+    const int my_rows = nrows > grp ? (nrows - grp + G - 1) / G : 0;
+    auto src = [&](int i) {
+        return reinterpret_cast<const uint4*>(p.w) + (static_cast<size_t>(r0 + grp + i * G) * p.N + col);
+    };
+    auto slot = [&](int i) { return smem_addr(ring + (i % D) * kThreads + tid); };
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        if (i < my_rows && col_ok) cp_async16(slot(i), src(i));
+        cp_async_commit();
+    }
+
+    // x'[m][k] = x[m][k] * gamma[k] * s[k] (times the int4 nibble scale);
+    // per vector: sum of squares, zero-point constant sum_k x gamma z.
+    pdl_wait();
+    float ss[M], cz[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) ss[m] = cz[m] = 0.f;
+    for (int e = tid; e < nk; e += kThreads) {
+        const int k = r0 * KPC + e;
+        const float g = NORM ? __ldg(p.gamma + k) : 1.f;
+        const float sc = kQuant ? __ldg(p.s + sblk + k) : 1.f;
+        const float zz = kQuant ? __ldg(p.z + sblk + k) : 0.f;
+        const int rl = e / KPC, i = e % KPC;
+        const float pre = BITS == 4 ? int4_prescale(i) : 1.f;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float xv = p.x[static_cast<size_t>(m) * p.K + k];
+            if (NORM) ss[m] = fmaf(xv, xv, ss[m]);
+            const float xg = xv * g;
+            if (kQuant) cz[m] = fmaf(xg, zz, cz[m]);
+            xs[(rl * M + m) * KPC + i] = xg * sc * pre;
+        }
+    }
+    __syncthreads();
+
+    uint64_t acc[M][4];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0ull;
+    for (int i = 0; i < my_rows; ++i) {
+        cp_async_wait<D - 1>();
+        const int rl = grp + i * G;
+        uint64_t w[NP];
+        decode_pairs<BITS>(ring[(i % D) * kThreads + tid], w);
+        const float4* xr = reinterpret_cast<const float4*>(xs + rl * M * KPC);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+#pragma unroll
+            for (int q = 0; q < NP; q += 2) {
+                const float4 xv = xr[(m * KPC + 2 * q) / 4];
+                acc[m][q & 3] = f2_fma(f2_pack(xv.x, xv.y), w[q], acc[m][q & 3]);
+                acc[m][(q + 1) & 3] = f2_fma(f2_pack(xv.z, xv.w), w[q + 1], acc[m][(q + 1) & 3]);
+            }
+        }
+        if (i + D < my_rows && col_ok) cp_async16(slot(i + D), src(i + D));
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const float2 a = f2_unpack(acc[m][0]), b = f2_unpack(acc[m][1]);
+        const float2 c2 = f2_unpack(acc[m][2]), d = f2_unpack(acc[m][3]);
+        red[m][tid] = ((a.x + a.y) + (b.x + b.y)) + ((c2.x + c2.y) + (d.x + d.y));
+        const float w0 = warp_sum(ss[m]), w1 = warp_sum(cz[m]);
+        if (lane == 0) {
+            wred[warp][2 * m] = w0;
+            wred[warp][2 * m + 1] = w1;
+        }
+    }
+    __syncthreads();
+
+    // cluster reduce-scatter: rank d finalises columns [d*share, (d+1)*share);
+    // every rank stores its partials for those columns, and its 2M scalars,
+    // into slot `rank` of rank d's receive buffer [S][M*share + 2M], then
+    // arrives on d's barrier; each rank adds the S slots in rank order.
+    if (S > 1) cluster_wait_acquire();  // every rank's barrier is initialised
+    const int share = (C + S - 1) / S;
+    const int rstride = M * share + 2 * M;
+    const uint32_t my_slot = smem_addr(rbuf) + static_cast<uint32_t>(rank * rstride * 4);
+    if (tid < C) {
+        const int dest = tid / share, cl = tid % share;
+        const uint32_t dst = dest == rank ? my_slot : map_cluster_addr(my_slot, dest);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float v = 0.f;
+            for (int g = 0; g < G; ++g) v += red[m][g * C + tid];
+            if (dest == rank) rbuf[rank * rstride + m * share + cl] = v;
+            else st_cluster_f32(dst + 4u * (m * share + cl), v);
+        }
+    }
+    if (tid < 2 * M) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) v += wred[w][tid];
+        for (int d = 0; d < S; ++d) {
+            if (d == rank) rbuf[rank * rstride + M * share + tid] = v;
+            else st_cluster_f32(map_cluster_addr(my_slot, d) + 4u * (M * share + tid), v);
+        }
+    }
+    __syncthreads();
+    if (S > 1 && tid == 0) {
+        fence_acq_rel_cluster();
+        for (int d = 0; d < S; ++d)
+            if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(&red_bar), d));
+        bool ok = false;
+        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
+        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
+    }
+    __syncthreads();
+    const int cc = rank * share + tid;
+    if (tid < share && cc < C && col0 + cc < p.N) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float a = 0.f, sq = 0.f, zc = 0.f;
+            for (int q = 0; q < S; ++q) {
+                const float* rp = rbuf + q * rstride;
+                a += rp[m * share + tid];
+                sq += rp[M * share + 2 * m];
+                zc += rp[M * share + 2 * m + 1];
+            }
+            const float inv = NORM ? 1.0f / sqrtf(sq * p.inv_dim + p.eps) : 1.0f;
+            p.y[static_cast<size_t>(m) * p.N + col0 + cc] = (kQuant ? a - zc : a) * inv;
+        }
+    }
+}
+
 struct DeviceInfo {
     int sms = 0;
 };
@@ -548,7 +770,7 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
         return set_error(kErrUnsupported, "K=%d is too long for one launch (%zu bytes of staged activations)", p.K,
                          smem);
     auto go = [&](auto kern) -> int {
-        if (smem > 48 * 1024)
+        if (smem > 40 * 1024)  // with the static part (about 3.3 KB), above 48 KB needs the opt-in
             if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
@@ -571,6 +793,87 @@ int launch_mode(int bits, const GemvParams& p, cudaStream_t s) {
         case 16: return launch_one<16, MODE>(p, s);
         case 8: return launch_one<8, MODE>(p, s);
         case 4: return launch_one<4, MODE>(p, s);
+    }
+    return set_error(kErrArg, "unsupported weight width %d (expected 32, 16, 8 or 4)", bits);
+}
+
+template <int BITS, int M>
+int launch_batched(const BatchParams& p0, bool norm, cudaStream_t stream) {
+    constexpr int KPC = 128 / BITS;
+    BatchParams p = p0;
+    p.R = p.K / KPC;
+    int sms = 0;
+    if (int e = sm_count(&sms)) return e;
+    // One wave: the most CTAs (C outputs x S-way split K, any S <= 8) that are
+    // all resident at once, at two CTAs per SM (the kernel's register budget)
+    // when their shared memory allows; wider tiles first on ties.
+    auto rbuf_floats = [&](int cw, int s) {
+        return (static_cast<size_t>(s) * (M * ((cw + s - 1) / s) + 2 * M) + 3) / 4 * 4;
+    };
+    auto smem_for = [&](int cw, int s) {
+        const int rows = (p.R + s - 1) / s;
+        return 32768 + (rbuf_floats(cw, s) + static_cast<size_t>(rows) * M * KPC) * 4;
+    };
+    int C = 32, S = 1;
+    long long best = -1;
+    for (int cw = 256; cw >= 32; cw /= 2)
+        for (int s = 1; s <= 8; ++s) {
+            const int rows = (p.R + s - 1) / s;
+            if ((s - 1) * rows >= p.R) continue;  // no empty ranks
+            const size_t sm = smem_for(cw, s);
+            const int occ = 2 * (sm + 9 * 1024) <= 227 * 1024 ? 2 : 1;
+            const long long ctas = static_cast<long long>((p.N + cw - 1) / cw) * s;
+            if (ctas <= static_cast<long long>(occ) * sms && ctas > best) {
+                best = ctas;
+                C = cw;
+                S = s;
+            }
+        }
+    p.rows_cta = (p.R + S - 1) / S;
+    p.cols = C;
+    p.rbuf_floats = static_cast<int>(rbuf_floats(C, S));
+    const size_t smem = smem_for(C, S);
+    if (smem > 200 * 1024)
+        return set_error(kErrUnsupported, "K=%d with %d vectors stages too many activations (%zu bytes)", p.K, M, smem);
+    auto go = [&](auto kern) -> int {
+        // dynamic + static shared memory above 48 KB needs the opt-in (the
+        // static part is up to 9 KB here)
+        if (smem > 36 * 1024)
+            if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, (p.N + C - 1) / C, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attrs[2];
+        cfg.attrs = attrs;
+        cfg.numAttrs = launch_attrs(attrs, S);
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+        return kOk;
+    };
+    return norm ? go(gemv_batched_kernel<BITS, M, true>) : go(gemv_batched_kernel<BITS, M, false>);
+}
+
+template <int BITS>
+int launch_batched_m(const BatchParams& p, int M, bool norm, cudaStream_t s) {
+    switch (M) {
+        case 2: return launch_batched<BITS, 2>(p, norm, s);
+        case 3: return launch_batched<BITS, 3>(p, norm, s);
+        case 4: return launch_batched<BITS, 4>(p, norm, s);
+        case 5: return launch_batched<BITS, 5>(p, norm, s);
+        case 6: return launch_batched<BITS, 6>(p, norm, s);
+        case 7: return launch_batched<BITS, 7>(p, norm, s);
+        case 8: return launch_batched<BITS, 8>(p, norm, s);
+    }
+    return set_error(kErrArg, "M=%d vectors (expected 1..%d)", M, kMaxBatch);
+}
+
+int launch_batched_bits(int bits, const BatchParams& p, int M, bool norm, cudaStream_t s) {
+    switch (bits) {
+        case 32: return launch_batched_m<32>(p, M, norm, s);
+        case 16: return launch_batched_m<16>(p, M, norm, s);
+        case 8: return launch_batched_m<8>(p, M, norm, s);
+        case 4: return launch_batched_m<4>(p, M, norm, s);
     }
     return set_error(kErrArg, "unsupported weight width %d (expected 32, 16, 8 or 4)", bits);
 }
@@ -804,6 +1107,45 @@ int vkc_rmsnorm_swiglu_peer(int bits, const void* wg, const float* sg, const flo
                             const float* gamma, float* h, int N, int K, float eps, int rms_dim, void* stream) {
     if (!in) return set_error(kErrArg, "null peer input");
     return swiglu_impl(bits, wg, sg, zg, wu, su, zu, x_base, gamma, h, N, K, eps, rms_dim, stream, in);
+}
+
+int vkc_gemv_batched(int bits, const void* w, const float* scale, const float* zero, const float* x, float* y,
+                     int M, int N, int K, void* stream) {
+    if (M < 1 || M > kMaxBatch) return set_error(kErrArg, "M=%d vectors (expected 1..%d)", M, kMaxBatch);
+    if (M == 1) return vkc_gemv(bits, w, scale, zero, x, y, N, K, stream);
+    if (int e = check_common(bits, N, K, w, scale, zero, x, y, nullptr)) return e;
+    if (K % 4 != 0) return set_error(kErrArg, "K=%d must be a multiple of 4 for batched rows", K);
+    BatchParams p = {};
+    p.w = static_cast<const uint8_t*>(w);
+    p.s = scale;
+    p.z = zero;
+    p.x = x;
+    p.y = y;
+    p.N = N;
+    p.K = K;
+    return launch_batched_bits(bits, p, M, false, static_cast<cudaStream_t>(stream));
+}
+
+int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                             const float* gamma, float* y, int M, int N, int K, float eps, int rms_dim,
+                             void* stream) {
+    if (M < 1 || M > kMaxBatch) return set_error(kErrArg, "M=%d vectors (expected 1..%d)", M, kMaxBatch);
+    if (M == 1) return vkc_rmsnorm_gemv(bits, w, scale, zero, x, gamma, y, N, K, eps, rms_dim, stream);
+    if (!gamma) return set_error(kErrArg, "null gamma");
+    if (int e = check_common(bits, N, K, w, scale, zero, x, y, gamma)) return e;
+    if (rms_dim <= 0) return set_error(kErrArg, "rms_dim=%d must be positive", rms_dim);
+    BatchParams p = {};
+    p.w = static_cast<const uint8_t*>(w);
+    p.s = scale;
+    p.z = zero;
+    p.x = x;
+    p.gamma = gamma;
+    p.y = y;
+    p.N = N;
+    p.K = K;
+    p.eps = eps;
+    p.inv_dim = 1.0f / static_cast<float>(rms_dim);
+    return launch_batched_bits(bits, p, M, true, static_cast<cudaStream_t>(stream));
 }
 
 // Status word of the current device (bits: kStatus*).  Reading waits for the

@@ -131,6 +131,25 @@ def gemv(w: PackedWeight, x: torch.Tensor, out=None, stream=None) -> torch.Tenso
     return y
 
 
+def gemv_batched(w: PackedWeight, x: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    """y[m] = W^T x[m] for the rows of x ([M][K], M <= 8), weights read once."""
+    M = x.shape[0]
+    y = out if out is not None else torch.empty(M, w.N, dtype=torch.float32, device=x.device)
+    check(lib().vkc_gemv_batched(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(y), M, w.N, w.K,
+                                 _s(stream)))
+    return y
+
+
+def rmsnorm_gemv_batched(w: PackedWeight, x: torch.Tensor, gamma, eps: float = 1e-6, rms_dim: int | None = None,
+                         out=None, stream=None) -> torch.Tensor:
+    """RmsNorm-GEMV of each row of x ([M][K], M <= 8), weights read once."""
+    M = x.shape[0]
+    y = out if out is not None else torch.empty(M, w.N, dtype=torch.float32, device=x.device)
+    check(lib().vkc_rmsnorm_gemv_batched(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma), _p(y),
+                                         M, w.N, w.K, eps, rms_dim or w.K, _s(stream)))
+    return y
+
+
 def gemv_residual(w: PackedWeight, x: torch.Tensor, residual: torch.Tensor, out=None, stream=None) -> torch.Tensor:
     """y = W^T x + residual."""
     y = _out(w.N, x, out)
