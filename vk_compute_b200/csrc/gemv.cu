@@ -39,6 +39,7 @@
 #include <cuda_fp16.h>
 
 #include <mutex>
+#include <vector>
 
 namespace vkc {
 
@@ -121,7 +122,6 @@ __device__ __forceinline__ float int4_prescale(int t) {
 }
 
 constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
-__device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(kMagic | bits); }
 
 // Two exact codes as an f32x2 pair (2^23 + code, both halves built in one asm
 // block so the pair lands in a register pair without moves).  int4: each half
@@ -715,6 +715,278 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_kernel(const BatchPa
     }
 }
 
+// ---- Batched decode on the tensor cores (int8 / int4 weights) ------------
+// mma.sync m16n8k16 with 16 weight columns as the M dimension (A: the codes as
+// fp16, exact) and the (up to 8) vectors as N (B: x' = x gamma s scaled by a
+// per-CTA power of two and split into fp16 high and low parts, two MMAs,
+// about 22 significant bits; fp32 accumulation).  Inside every 16-byte chunk
+// the k order is permuted so that lane (g, t4) of a warp reads one 32-bit
+// word per column, bytes [4 t4, 4 t4 + 4); the staged B fragments follow the
+// same permutation (a dot product does not depend on the order).  A warp owns
+// 64 columns and every RG-th chunk row of the CTA's K slice, and streams them
+// through its own cp.async ring (warps never wait for each other while
+// streaming).  About 1.5 instructions per weight for any batch, against
+// 5-10 for the SIMT kernel.  The epilogue is the SIMT batched kernel's
+// cluster reduce-scatter.
+constexpr int kMmaRing = 8;  // chunk rows in flight per warp (1 KB each)
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ void mma16816_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hsub_1024(uint32_t h) {
+    uint32_t d;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(h), "r"(0x64006400u));
+    return d;
+}
+// int8: bytes (0,1) or (2,3) of w as an exact fp16 pair
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t byte_h2(uint32_t w) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(w), "r"(0x64646464u), "n"(SEL));
+    return hsub_1024(d);
+}
+// int4: nibbles (j, j + 4) of w as an exact fp16 pair
+__device__ __forceinline__ uint32_t nib_h2(uint32_t w, int j) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w >> (4 * j)), "r"(0x000F000Fu), "r"(0x64006400u));
+    return hsub_1024(d);
+}
+
+template <int BITS, bool NORM>
+__global__ void __launch_bounds__(kThreads, 2) gemv_batched_mma_kernel(const BatchParams p, const int M) {
+    constexpr int KPC = 128 / BITS;
+    constexpr int STEPS = KPC / 16;   // k16 steps per chunk: int8 1, int4 2
+    constexpr int FRAG = 4 * STEPS;   // staged u32 per (row, vector, t4): {hi b0, hi b1, lo b0, lo b1} per step
+    static_assert(BITS == 8 || BITS == 4, "tensor-core batched decode: int8 / int4 codes");
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* ring = reinterpret_cast<uint4*>(smem);                                   // [8 warps][kMmaRing][64]
+    float* rbuf = reinterpret_cast<float*>(smem + 8 * kMmaRing * 64 * 16);          // reduce-scatter slots
+    uint32_t* bfr = reinterpret_cast<uint32_t*>(rbuf + p.rbuf_floats);              // [rows][8][4][FRAG]
+    float* red = reinterpret_cast<float*>(smem);  // after streaming: [RG][8][C] over the ring
+    __shared__ float wred[kThreads / 32][2 * kMaxBatch];
+    __shared__ float s_amax[kThreads / 32];
+    __shared__ __align__(8) uint64_t red_bar;
+
+    uint32_t nctarank, ctarank;
+    asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(nctarank));
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(ctarank));
+    const int S = static_cast<int>(nctarank);
+    const int rank = static_cast<int>(ctarank);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int C = p.cols, NCG = C / 64, RG = 8 / NCG;
+    const int cg = warp % NCG, rg = warp / NCG;
+    const int col0 = blockIdx.y * C;
+    const int r0 = rank * p.rows_cta;
+    const int nrows = max(0, min(p.rows_cta, p.R - r0));
+    const int nk = nrows * KPC;
+    const size_t sblk = static_cast<size_t>(col0 / kGroup) * p.K;
+
+    if (S > 1) {
+        if (tid == 0) {
+            mbar_init(smem_addr(&red_bar), static_cast<uint32_t>(S - 1));
+            mbar_init_fence();
+        }
+        cluster_arrive_release();
+    }
+    pdl_launch_dependents();
+
+    // weights first: this warp's rows rg, rg + RG, ... of its 64 columns
+    uint4* wring = ring + warp * kMmaRing * 64;
+    const int my_rows = nrows > rg ? (nrows - rg + RG - 1) / RG : 0;
+    const uint4* wsrc = reinterpret_cast<const uint4*>(p.w) + col0 + cg * 64 + lane;
+    auto copy_row = [&](int i) {
+        const size_t r = static_cast<size_t>(r0 + rg + i * RG);
+        const uint32_t dst = smem_addr(wring + (i % kMmaRing) * 64 + lane);
+        cp_async16(dst, wsrc + r * p.N);
+        cp_async16(dst + 32 * 16, wsrc + r * p.N + 32);
+    };
+#pragma unroll
+    for (int i = 0; i < kMmaRing; ++i) {
+        if (i < my_rows) copy_row(i);
+        cp_async_commit();
+    }
+
+    // x' = x gamma s for this CTA's k slice: a per-CTA power of two brings its
+    // largest magnitude to [2^14, 2^15), then each value is split into fp16
+    // high + low parts in the B-fragment order of the permuted k.
+    pdl_wait();
+    float amax = 0.f;
+    for (int e = tid; e < nk; e += kThreads) {
+        const int k = r0 * KPC + e;
+        const float gs = (NORM ? __ldg(p.gamma + k) : 1.f) * __ldg(p.s + sblk + k);
+        for (int m = 0; m < M; ++m) amax = fmaxf(amax, fabsf(p.x[static_cast<size_t>(m) * p.K + k] * gs));
+    }
+    amax = warp_max(amax);
+    if (lane == 0) s_amax[warp] = amax;
+    __syncthreads();
+    amax = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) amax = fmaxf(amax, s_amax[w]);
+    int ex = 0;
+    if (amax > 0.f) ex = 14 - (((__float_as_int(amax) >> 23) & 0xFF) - 127);
+    ex = max(-100, min(100, ex));
+    const float up = ldexpf(1.0f, ex), down = ldexpf(1.0f, -ex);
+
+    float ss[kMaxBatch], cz[kMaxBatch];
+#pragma unroll
+    for (int m = 0; m < kMaxBatch; ++m) ss[m] = cz[m] = 0.f;
+    __half* bh = reinterpret_cast<__half*>(bfr);
+    for (int e = tid; e < nk; e += kThreads) {
+        const int k = r0 * KPC + e;
+        const float gm = NORM ? __ldg(p.gamma + k) : 1.f;
+        const float sc = __ldg(p.s + sblk + k), zz = __ldg(p.z + sblk + k);
+        const int rl = e / KPC, i = e % KPC;
+        int tq, u, half;  // lane t4, u32 index (hi part) within FRAG, half
+        if (BITS == 8) {
+            tq = i >> 2;
+            u = (i >> 1) & 1;
+            half = i & 1;
+        } else {
+            tq = i >> 3;
+            const int nib = i & 7, j = nib & 3;
+            u = (j >> 1) * 4 + (j & 1);
+            half = nib >> 2;
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxBatch; ++m) {
+            float v = 0.f;
+            if (m < M) {
+                const float xv = p.x[static_cast<size_t>(m) * p.K + k];
+                if (NORM) ss[m] = fmaf(xv, xv, ss[m]);
+                const float xg = xv * gm;
+                cz[m] = fmaf(xg, zz, cz[m]);
+                v = xg * sc * up;
+            }
+            const __half hi = __float2half_rn(v);
+            const __half lo = __float2half_rn(v - __half2float(hi));
+            const size_t base = ((static_cast<size_t>(rl) * 8 + m) * 4 + tq) * FRAG;
+            bh[(base + u) * 2 + half] = hi;
+            bh[(base + u + 2) * 2 + half] = lo;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxBatch; ++m) {
+        const float w0 = warp_sum(ss[m]), w1 = warp_sum(cz[m]);
+        if (lane == 0) {
+            wred[warp][2 * m] = w0;
+            wred[warp][2 * m + 1] = w1;
+        }
+    }
+    __syncthreads();
+
+    // stream: per row, 4 tiles of 16 columns x 16 (or 2 x 16) k
+    float acc[4][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+    for (int i = 0; i < my_rows; ++i) {
+        cp_async_wait<kMmaRing - 1>();
+        __syncwarp();
+        const uint32_t* rowp = reinterpret_cast<const uint32_t*>(wring + (i % kMmaRing) * 64);
+        const int rl = rg + i * RG;
+        const uint4* bq = reinterpret_cast<const uint4*>(bfr + ((static_cast<size_t>(rl) * 8 + g) * 4 + t4) * FRAG);
+        const uint4 b0 = bq[0];
+        uint4 b1 = b0;
+        if constexpr (STEPS == 2) b1 = bq[1];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t wa = rowp[(t * 16 + g) * 4 + t4];
+            const uint32_t wb = rowp[(t * 16 + g + 8) * 4 + t4];
+            if constexpr (BITS == 8) {
+                const uint32_t a[4] = {byte_h2<0x4140>(wa), byte_h2<0x4140>(wb), byte_h2<0x4342>(wa),
+                                       byte_h2<0x4342>(wb)};
+                mma16816_f16(acc[t], a, b0.x, b0.y);
+                mma16816_f16(acc[t], a, b0.z, b0.w);
+            } else {
+                const uint32_t a[4] = {nib_h2(wa, 0), nib_h2(wb, 0), nib_h2(wa, 1), nib_h2(wb, 1)};
+                mma16816_f16(acc[t], a, b0.x, b0.y);
+                mma16816_f16(acc[t], a, b0.z, b0.w);
+                const uint32_t a2[4] = {nib_h2(wa, 2), nib_h2(wb, 2), nib_h2(wa, 3), nib_h2(wb, 3)};
+                mma16816_f16(acc[t], a2, b1.x, b1.y);
+                mma16816_f16(acc[t], a2, b1.z, b1.w);
+            }
+        }
+        __syncwarp();  // every lane has read the slot before it is refilled
+        if (i + kMmaRing < my_rows) copy_row(i + kMmaRing);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is free: row-group partials go over it
+
+    // D fragment of tile t: (column g, vectors 2t4, 2t4+1), (column g+8, same)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int c = cg * 64 + t * 16 + g;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = 2 * t4 + h;
+            red[(rg * 8 + m) * C + c] = acc[t][h] * down;
+            red[(rg * 8 + m) * C + c + 8] = acc[t][2 + h] * down;
+        }
+    }
+    __syncthreads();
+
+    // cluster reduce-scatter (as gemv_batched_kernel)
+    if (S > 1) cluster_wait_acquire();
+    const int share = (C + S - 1) / S;
+    const int rstride = kMaxBatch * share + 2 * kMaxBatch;
+    const uint32_t my_slot = smem_addr(rbuf) + static_cast<uint32_t>(rank * rstride * 4);
+    if (tid < C) {
+        const int dest = tid / share, cl = tid % share;
+        const uint32_t dst = dest == rank ? my_slot : map_cluster_addr(my_slot, dest);
+        for (int m = 0; m < M; ++m) {
+            float v = 0.f;
+            for (int q = 0; q < RG; ++q) v += red[(q * 8 + m) * C + tid];
+            if (dest == rank) rbuf[rank * rstride + m * share + cl] = v;
+            else st_cluster_f32(dst + 4u * (m * share + cl), v);
+        }
+    }
+    if (tid < 2 * kMaxBatch) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) v += wred[w][tid];
+        for (int d = 0; d < S; ++d) {
+            if (d == rank) rbuf[rank * rstride + kMaxBatch * share + tid] = v;
+            else st_cluster_f32(map_cluster_addr(my_slot, d) + 4u * (kMaxBatch * share + tid), v);
+        }
+    }
+    __syncthreads();
+    if (S > 1 && tid == 0) {
+        fence_acq_rel_cluster();
+        for (int d = 0; d < S; ++d)
+            if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(&red_bar), d));
+        bool ok = false;
+        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
+        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
+    }
+    __syncthreads();
+    const int cc = rank * share + tid;
+    if (tid < share && cc < C && col0 + cc < p.N) {
+        for (int m = 0; m < M; ++m) {
+            float a = 0.f, sq = 0.f, zc = 0.f;
+            for (int q = 0; q < S; ++q) {
+                const float* rp = rbuf + q * rstride;
+                a += rp[m * share + tid];
+                sq += rp[kMaxBatch * share + 2 * m];
+                zc += rp[kMaxBatch * share + 2 * m + 1];
+            }
+            const float inv = NORM ? 1.0f / sqrtf(sq * p.inv_dim + p.eps) : 1.0f;
+            p.y[static_cast<size_t>(m) * p.N + col0 + cc] = (a - zc) * inv;
+        }
+    }
+}
+
 struct DeviceInfo {
     int sms = 0;
 };
@@ -854,6 +1126,109 @@ int launch_batched(const BatchParams& p0, bool norm, cudaStream_t stream) {
     return norm ? go(gemv_batched_kernel<BITS, M, true>) : go(gemv_batched_kernel<BITS, M, false>);
 }
 
+// Clusters of S CTAs of `func` with `smem` bytes each that can be resident at
+// once (cached per device): cluster placement inside the GPCs, not the SM
+// count, bounds one wave of a clustered launch.
+int max_clusters(const void* func, int S, size_t smem, int* out) {
+    struct Entry {
+        int dev;
+        const void* func;
+        int S;
+        size_t smem;
+        int n;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    VKC_CUDA_TRY(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry& e : cache)
+            if (e.dev == dev && e.func == func && e.S == S && e.smem == smem) {
+                *out = e.n;
+                return kOk;
+            }
+    }
+    if (int e = ensure_smem(func, smem)) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = S;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    VKC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, func, &cfg));
+    std::lock_guard<std::mutex> lock(mu);
+    cache.push_back({dev, func, S, smem, n});
+    *out = n;
+    return kOk;
+}
+
+template <int BITS>
+int launch_batched_mma(const BatchParams& p0, int M, bool norm, cudaStream_t stream) {
+    constexpr int KPC = 128 / BITS;
+    constexpr int FRAG = 4 * (KPC / 16);
+    BatchParams p = p0;
+    p.R = p.K / KPC;
+    int sms = 0;
+    if (int e = sm_count(&sms)) return e;
+    auto rbuf_floats = [&](int cw, int s) {
+        return (static_cast<size_t>(s) * (kMaxBatch * ((cw + s - 1) / s) + 2 * kMaxBatch) + 3) / 4 * 4;
+    };
+    auto smem_for = [&](int cw, int s) {
+        const size_t rows = static_cast<size_t>((p.R + s - 1) / s);
+        return static_cast<size_t>(8 * kMmaRing * 64 * 16) + rbuf_floats(cw, s) * 4 + rows * 8 * 4 * FRAG * 4;
+    };
+    // one wave: the most CTAs whose clusters are all resident at once (as the
+    // occupancy calculator places them), wider tiles first on ties
+    const void* kern = norm ? reinterpret_cast<const void*>(gemv_batched_mma_kernel<BITS, true>)
+                            : reinterpret_cast<const void*>(gemv_batched_mma_kernel<BITS, false>);
+    int C = 64, S = 1;
+    long long best = -1;
+    for (int cw = 256; cw >= 64; cw /= 2) {
+        if (p.N % cw) continue;
+        for (int s = 1; s <= 8; ++s) {
+            const int rows = (p.R + s - 1) / s;
+            if ((s - 1) * rows >= p.R) continue;
+            const size_t sm = smem_for(cw, s);
+            if (sm > 200 * 1024) continue;
+            const long long ctas = static_cast<long long>(p.N / cw) * s;
+            if (ctas <= best || ctas > 2LL * sms) continue;
+            int nc = 0;
+            if (int e = max_clusters(kern, s, sm, &nc)) return e;
+            if (ctas <= static_cast<long long>(nc) * s) {
+                best = ctas;
+                C = cw;
+                S = s;
+            }
+        }
+    }
+    if (best < 0) return set_error(kErrUnsupported, "K=%d stages too many activations for a batched launch", p.K);
+    p.rows_cta = (p.R + S - 1) / S;
+    p.cols = C;
+    p.rbuf_floats = static_cast<int>(rbuf_floats(C, S));
+    const size_t smem = smem_for(C, S);
+    auto go = [&](auto kern) -> int {
+        if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, p.N / C, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attrs[2];
+        cfg.attrs = attrs;
+        cfg.numAttrs = launch_attrs(attrs, S);
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, M));
+        return kOk;
+    };
+    return norm ? go(gemv_batched_mma_kernel<BITS, true>) : go(gemv_batched_mma_kernel<BITS, false>);
+}
+
 template <int BITS>
 int launch_batched_m(const BatchParams& p, int M, bool norm, cudaStream_t s) {
     switch (M) {
@@ -868,12 +1243,15 @@ int launch_batched_m(const BatchParams& p, int M, bool norm, cudaStream_t s) {
     return set_error(kErrArg, "M=%d vectors (expected 1..%d)", M, kMaxBatch);
 }
 
+// Quantised weights run on the tensor cores when N is a multiple of 64 (always,
+// as their scale blocks are 256 outputs); fp16 / fp32 weights on the SIMT kernel.
 int launch_batched_bits(int bits, const BatchParams& p, int M, bool norm, cudaStream_t s) {
+    const bool use_mma = p.N % 64 == 0;
     switch (bits) {
         case 32: return launch_batched_m<32>(p, M, norm, s);
         case 16: return launch_batched_m<16>(p, M, norm, s);
-        case 8: return launch_batched_m<8>(p, M, norm, s);
-        case 4: return launch_batched_m<4>(p, M, norm, s);
+        case 8: return use_mma ? launch_batched_mma<8>(p, M, norm, s) : launch_batched_m<8>(p, M, norm, s);
+        case 4: return use_mma ? launch_batched_mma<4>(p, M, norm, s) : launch_batched_m<4>(p, M, norm, s);
     }
     return set_error(kErrArg, "unsupported weight width %d (expected 32, 16, 8 or 4)", bits);
 }
