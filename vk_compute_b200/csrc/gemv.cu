@@ -818,15 +818,56 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_mma_kernel(const Bat
         cp_async_commit();
     }
 
-    // x' = x gamma s for this CTA's k slice: a per-CTA power of two brings its
-    // largest magnitude to [2^14, 2^15), then each value is split into fp16
-    // high + low parts in the B-fragment order of the permuted k.
+    // x' = x gamma s for this CTA's k slice.  Pass 1 stores it as fp32 in the
+    // staging area in natural order, [row][vector][KPC] (the same bytes the
+    // fragments take), with the sums of squares, zero-point constants and the
+    // largest magnitude; pass 2 rewrites each (row, vector) block in place --
+    // one thread per block -- as the permuted fp16 high/low fragments, scaled
+    // by the per-CTA power of two that brings the magnitude to [2^14, 2^15).
     pdl_wait();
+    float ss[kMaxBatch], cz[kMaxBatch];
+#pragma unroll
+    for (int m = 0; m < kMaxBatch; ++m) ss[m] = cz[m] = 0.f;
     float amax = 0.f;
-    for (int e = tid; e < nk; e += kThreads) {
-        const int k = r0 * KPC + e;
-        const float gs = (NORM ? __ldg(p.gamma + k) : 1.f) * __ldg(p.s + sblk + k);
-        for (int m = 0; m < M; ++m) amax = fmaxf(amax, fabsf(p.x[static_cast<size_t>(m) * p.K + k] * gs));
+    float* xf = reinterpret_cast<float*>(bfr);
+    constexpr int U = 2;
+    for (int e0 = tid; e0 < nk; e0 += U * kThreads) {
+        float gm[U], sc[U], zz[U], xv[U][kMaxBatch];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int e = e0 + u * kThreads;
+            const bool ok = e < nk;
+            const int k = r0 * KPC + (ok ? e : 0);
+            gm[u] = (NORM && ok) ? __ldg(p.gamma + k) : 1.f;
+            sc[u] = ok ? __ldg(p.s + sblk + k) : 0.f;
+            zz[u] = ok ? __ldg(p.z + sblk + k) : 0.f;
+#pragma unroll
+            for (int m = 0; m < kMaxBatch; ++m)
+                xv[u][m] = (ok && m < M) ? __ldg(p.x + static_cast<size_t>(m) * p.K + k) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int e = e0 + u * kThreads;
+            if (e >= nk) continue;
+            const int rl = e / KPC, i = e % KPC;
+#pragma unroll
+            for (int m = 0; m < kMaxBatch; ++m) {
+                const float xg = xv[u][m] * gm[u];
+                if (NORM) ss[m] = fmaf(xv[u][m], xv[u][m], ss[m]);
+                cz[m] = fmaf(xg, zz[u], cz[m]);
+                const float v = xg * sc[u];
+                amax = fmaxf(amax, fabsf(v));
+                xf[(rl * 8 + m) * KPC + i] = v;
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxBatch; ++m) {
+        const float w0 = warp_sum(ss[m]), w1 = warp_sum(cz[m]);
+        if (lane == 0) {
+            wred[warp][2 * m] = w0;
+            wred[warp][2 * m + 1] = w1;
+        }
     }
     amax = warp_max(amax);
     if (lane == 0) s_amax[warp] = amax;
@@ -839,50 +880,52 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_mma_kernel(const Bat
     ex = max(-100, min(100, ex));
     const float up = ldexpf(1.0f, ex), down = ldexpf(1.0f, -ex);
 
-    float ss[kMaxBatch], cz[kMaxBatch];
+    // pass 2: blocks of vectors m >= M are zero, which is also their fragment
+    for (int blk = tid; blk < nrows * 8; blk += kThreads) {
+        const int m = blk & 7;
+        if (m >= M) continue;
+        float4* bp = reinterpret_cast<float4*>(xf + blk * KPC);
+        float v[KPC];
 #pragma unroll
-    for (int m = 0; m < kMaxBatch; ++m) ss[m] = cz[m] = 0.f;
-    __half* bh = reinterpret_cast<__half*>(bfr);
-    for (int e = tid; e < nk; e += kThreads) {
-        const int k = r0 * KPC + e;
-        const float gm = NORM ? __ldg(p.gamma + k) : 1.f;
-        const float sc = __ldg(p.s + sblk + k), zz = __ldg(p.z + sblk + k);
-        const int rl = e / KPC, i = e % KPC;
-        int tq, u, half;  // lane t4, u32 index (hi part) within FRAG, half
-        if (BITS == 8) {
-            tq = i >> 2;
-            u = (i >> 1) & 1;
-            half = i & 1;
-        } else {
-            tq = i >> 3;
-            const int nib = i & 7, j = nib & 3;
-            u = (j >> 1) * 4 + (j & 1);
-            half = nib >> 2;
+        for (int q = 0; q < KPC / 4; ++q) {
+            const float4 f = bp[q];
+            v[4 * q] = f.x * up;
+            v[4 * q + 1] = f.y * up;
+            v[4 * q + 2] = f.z * up;
+            v[4 * q + 3] = f.w * up;
         }
+        uint32_t fr[4][FRAG];  // [t4][u32]
 #pragma unroll
-        for (int m = 0; m < kMaxBatch; ++m) {
-            float v = 0.f;
-            if (m < M) {
-                const float xv = p.x[static_cast<size_t>(m) * p.K + k];
-                if (NORM) ss[m] = fmaf(xv, xv, ss[m]);
-                const float xg = xv * gm;
-                cz[m] = fmaf(xg, zz, cz[m]);
-                v = xg * sc * up;
+        for (int i = 0; i < KPC; ++i) {
+            int tq, u, half;
+            if (BITS == 8) {
+                tq = i >> 2;
+                u = (i >> 1) & 1;
+                half = i & 1;
+            } else {
+                tq = i >> 3;
+                const int nib = i & 7, j = nib & 3;
+                u = (j >> 1) * 4 + (j & 1);
+                half = nib >> 2;
             }
-            const __half hi = __float2half_rn(v);
-            const __half lo = __float2half_rn(v - __half2float(hi));
-            const size_t base = ((static_cast<size_t>(rl) * 8 + m) * 4 + tq) * FRAG;
-            bh[(base + u) * 2 + half] = hi;
-            bh[(base + u + 2) * 2 + half] = lo;
+            const __half hi = __float2half_rn(v[i]);
+            const __half lo = __float2half_rn(v[i] - __half2float(hi));
+            const uint32_t hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
+            if (half == 0) {
+                fr[tq][u] = hb;
+                fr[tq][u + 2] = lb;
+            } else {
+                fr[tq][u] |= hb << 16;
+                fr[tq][u + 2] |= lb << 16;
+            }
         }
-    }
+        uint4* op = reinterpret_cast<uint4*>(bp);
 #pragma unroll
-    for (int m = 0; m < kMaxBatch; ++m) {
-        const float w0 = warp_sum(ss[m]), w1 = warp_sum(cz[m]);
-        if (lane == 0) {
-            wred[warp][2 * m] = w0;
-            wred[warp][2 * m + 1] = w1;
-        }
+        for (int tq = 0; tq < 4; ++tq)
+#pragma unroll
+            for (int q = 0; q < FRAG / 4; ++q)
+                op[tq * (FRAG / 4) + q] =
+                    make_uint4(fr[tq][4 * q], fr[tq][4 * q + 1], fr[tq][4 * q + 2], fr[tq][4 * q + 3]);
     }
     __syncthreads();
 
