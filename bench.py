@@ -679,7 +679,8 @@ def main():
                "h2d_bytes_per_step": r["h2d_bytes_per_step"], "d2h_bytes_per_step": r["d2h_bytes_per_step"],
                "us_per_step": round(dt * 1e6, 2),
                "path": "C host (vkc_e2e_bench): writeBuffer + execute + readBuffer per step, reference ABI, "
-                       "host wall clock, weight pool > 4x L2"}
+                       "host wall clock, weight pool > 4x L2; execute timing events off (vkc_set_timing(0): "
+                       "the program never calls getExecutionTime)"}
     elif wl["e2e"] is not None:
         dt, hb, db = e2e_dropin(args, wl["e2e"], local)
         if world > 1:

@@ -39,7 +39,8 @@ typedef struct operation {
  * gives.  Unknown operator names, missing bindings and undersized buffers
  * print to stderr and exit, as the reference does on its fatal paths. */
 void execute(session s, operation ops[], int opCount);
-/* include/dispatch.h:26 -- device time of the last execute, in ms. */
+/* include/dispatch.h:26 -- device time of the last execute, in ms (0 when
+ * timing is off: vkc_set_timing in vk_compute_b200.h). */
 double getExecutionTime(session s);
 
 #endif

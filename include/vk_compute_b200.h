@@ -45,6 +45,13 @@ int vkc_version(void);
  * are visible. */
 void vkc_set_pdl(int enable);
 int vkc_get_pdl(void);
+/* Timing of execute() for getExecutionTime (1, the default, as in the
+ * reference) or none (0): every timed execute records two CUDA events around
+ * its operators, which costs host time and keeps the next kernel from
+ * starting early; a program that never calls getExecutionTime can turn it
+ * off, after which getExecutionTime returns 0. */
+void vkc_set_timing(int enable);
+int vkc_get_timing(void);
 /* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
 int vkc_has_operator(const char* shader);
 /* Waits for the current device and returns its status word: bit 0 set when a

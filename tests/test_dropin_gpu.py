@@ -130,3 +130,26 @@ def test_chained_ops_in_one_execute(sess):
     h = o.qgemv(x, None, d4, s4, z4, 4, K, K)
     ref = o.qgemv(h, g, d8, s8, z8, 8, K, N, 4096, 1e-5)
     assert_close(D.read_buffer(sess, y), ref, 5e-3, "chain")
+
+
+def test_timing_switch(sess):
+    """With execute() timing off, results are unchanged and getExecutionTime
+    returns 0; turned back on, it reports the device time again."""
+    x = host_vector(SEED_X, K)
+    w, sc, zr, host = packed(SEED_W, 8)
+    y = D.create_buffer(sess, None, 4 * N)
+    xb, wb, sb, zb = bufs(sess, x, w, sc, zr)
+    op = [D.operation("GEMV-INT8.spv", [xb, wb, y, sb, zb], [1, N, K])]
+    ref = o.qgemv(x, None, *host, 8, K, N)
+    from vk_compute_b200._lib import lib as vlib
+    try:
+        vlib().vkc_set_timing(0)
+        assert vlib().vkc_get_timing() == 0
+        assert D.execute(sess, op) == 0.0
+        assert_close(D.read_buffer(sess, y), ref, TOL[8], "GEMV-INT8, timing off")
+    finally:
+        vlib().vkc_set_timing(1)
+    assert D.execute(sess, op) > 0.0
+    assert_close(D.read_buffer(sess, y), ref, TOL[8], "GEMV-INT8, timing on")
+    for b in (xb, wb, sb, zb, y):
+        D.destroy_buffer(sess, b)

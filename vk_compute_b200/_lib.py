@@ -20,6 +20,8 @@ SIGNATURES = {
     "vkc_version": (_i, []),
     "vkc_set_pdl": (None, [_i]),
     "vkc_get_pdl": (_i, []),
+    "vkc_set_timing": (None, [_i]),
+    "vkc_get_timing": (_i, []),
     "vkc_has_operator": (_i, [C.c_char_p]),
     "vkc_device_status": (_i, [C.POINTER(C.c_uint), _i]),
     "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),

@@ -6,6 +6,8 @@
  *
  *   vkc_e2e_bench <op> <N> <K> <steps> <warmup>
  *   op: RmsNorm-GEMV-INT8 | GEMV-FP16
+ * The program never asks for getExecutionTime, so it turns execute()'s timing
+ * events off (vkc_set_timing(0)), as such a program would.
  * Prints one JSON object: us_per_step, h2d_bytes_per_step, d2h_bytes_per_step. */
 #include <stdint.h>
 #include <stdio.h>
@@ -15,6 +17,7 @@
 
 #include "dispatch.h"
 #include "session.h"
+#include "vk_compute_b200.h"
 
 static uint64_t rng = 0x9E3779B97F4A7C15ull;
 static uint32_t next_u32(void) {
@@ -50,6 +53,7 @@ int main(int argc, char** argv) {
     if (pool < 2) pool = 2;
     if (pool > 64) pool = 64;
 
+    vkc_set_timing(0);
     session s = createSession();
     uint8_t* hw = (uint8_t*)malloc(wbytes);
     float* hs = (float*)malloc(sbytes ? sbytes : 4);

@@ -35,6 +35,7 @@ namespace vkc {
 
 static thread_local char g_err[512] = "";
 static bool g_pdl = false;
+static bool g_timing = true;
 
 int set_error(int code, const char* fmt, ...) {
     va_list ap;
@@ -137,10 +138,12 @@ constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronous
 void stream_synced(Ctx* c) { c->stage_busy[0] = c->stage_busy[1] = false; }
 
 // Device -> mapped host copy for readBuffer: a kernel rather than a DMA copy
-// (lower latency for the kilobytes a decode step reads back).  Runs after the
-// previous kernel has completed (no early launch), so it sees its results.
+// (lower latency for the kilobytes a decode step reads back).  It may be
+// launched while the previous kernel still runs (programmatic dependent
+// launch) and reads only after that kernel's writes are visible.
 __global__ void download_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
                                 uint8_t* __restrict__ dst_tail, const uint8_t* __restrict__ src_tail, int tail) {
+    pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
     if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < tail) dst_tail[threadIdx.x] = src_tail[threadIdx.x];
@@ -152,10 +155,18 @@ cudaError_t launch_download(void* dst, const void* src, size_t n, cudaStream_t s
     int blocks = static_cast<int>((n16 + 255) / 256);
     if (blocks < 1) blocks = 1;
     if (blocks > 148) blocks = 148;
-    download_kernel<<<blocks, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
-                                                 static_cast<uint8_t*>(dst) + n16 * 16,
-                                                 static_cast<const uint8_t*>(src) + n16 * 16, tail);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;  // safe whatever vkc_set_pdl says: it waits first
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, download_kernel, static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
+                              static_cast<uint8_t*>(dst) + n16 * 16, static_cast<const uint8_t*>(src) + n16 * 16,
+                              tail);
 }
 constexpr uint32_t kCtxMagic = 0x564b4331u;  // "VKC1"
 
@@ -402,6 +413,8 @@ extern "C" {
 const char* vkc_last_error(void) { return g_err; }
 void vkc_set_pdl(int enable) { g_pdl = enable != 0; }
 int vkc_get_pdl(void) { return g_pdl ? 1 : 0; }
+void vkc_set_timing(int enable) { g_timing = enable != 0; }
+int vkc_get_timing(void) { return g_timing ? 1 : 0; }
 int vkc_version(void) { return VKC_VERSION; }
 
 // --- device.h --------------------------------------------------------------
@@ -563,11 +576,12 @@ void destroyBuffer(VkDevice dev, buffer buf) {
 void execute(session s, operation ops[], int opCount) {
     Ctx* c = ctx_of(s.dev.device);
     if (opCount < 0) fatal("execute: negative operation count");
-    check_cuda(cudaEventRecord(c->ev_begin, c->stream), "cudaEventRecord");
+    const bool timed = g_timing;
+    if (timed) check_cuda(cudaEventRecord(c->ev_begin, c->stream), "cudaEventRecord");
     for (int i = 0; i < opCount; ++i) run_op(c, ops[i]);
-    check_cuda(cudaEventRecord(c->ev_end, c->stream), "cudaEventRecord");
+    if (timed) check_cuda(cudaEventRecord(c->ev_end, c->stream), "cudaEventRecord");
     check_cuda(cudaGetLastError(), "execute");
-    c->timed = true;
+    c->timed = timed;
 }
 
 double getExecutionTime(session s) {
