@@ -188,6 +188,16 @@ int vkc_attention_decode_cache(const void* q, int q_bits, const void* kcache, co
                                float* out, int n_q, int n_kv, int head_dim, int ctx, int ctx_cap,
                                float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* vkc_attention_decode_cache for a decode step right after the KV append
+ * (vkc_rmsnorm_gemv_rope_kv at pos = ctx - 1): with programmatic dependent
+ * launch on, cache tokens [0, ctx - 1) are requested before the wait on the
+ * previous kernel, so the contract is that no kernel still running writes
+ * them (the previous kernel wrote only token ctx - 1).  A workspace is
+ * required. */
+int vkc_attention_decode_append(const void* q, int q_bits, const void* kcache, const void* vcache,
+                                float* out, int n_q, int n_kv, int head_dim, int ctx, int ctx_cap,
+                                float scale, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  * For callers that cannot allocate device memory when attention runs (an
  * engine whose memory pool already owns all of HBM, a decode loop that must not

@@ -103,3 +103,27 @@ def test_repeated_calls_reuse_workspace():
         assert_close(out.cpu().numpy(), ref, 2e-3, f"call {seed}")
     # tickets are left at zero for the next call
     assert int(ws[:4 * n_kv].view(torch.int32).abs().sum()) == 0
+
+
+@pytest.mark.parametrize("n_q,n_kv,hd,ctx", [(32, 8, 128, 8192), (4, 1, 128, 777), (8, 2, 64, 300), (16, 4, 128, 65)])
+def test_append_variant_matches(n_q, n_kv, hd, ctx):
+    """vkc_attention_decode_append (cache rows before the newest token requested
+    before the wait on the previous kernel) gives the same bits as the plain
+    cache entry, right after the newest token was written by a kernel."""
+    cap = ctx + 5
+    g = torch.Generator().manual_seed(ctx)
+    q = torch.randn(n_q * hd, generator=g).cuda()
+    kc = torch.randn(cap, n_kv, hd, generator=g).half().cuda()
+    vc = torch.randn(n_kv, hd // 8, cap, 8, generator=g).half().cuda()
+    ws = ops.attention_workspace(n_q, n_kv, hd, ctx)
+    newest_k = torch.randn(n_kv, hd, generator=g).half().cuda()
+    prev = ops.get_pdl()
+    ops.set_pdl(True)
+    try:
+        kc[ctx - 1].copy_(newest_k)  # the newest token, written by a kernel just before
+        a = ops.attention_decode(q, kc, vc, n_q, n_kv, hd, ctx, hd ** -0.5, workspace=ws, ctx_cap=cap,
+                                 after_append=True).clone()
+        b = ops.attention_decode(q, kc, vc, n_q, n_kv, hd, ctx, hd ** -0.5, workspace=ws, ctx_cap=cap)
+    finally:
+        ops.set_pdl(prev)
+    assert torch.equal(a, b)

@@ -33,6 +33,7 @@ SIGNATURES = {
     "vkc_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "vkc_attention_decode": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_attention_decode_cache": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
+    "vkc_attention_decode_append": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_gemm_f32": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "vkc_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "vkc_gemm_bf16_status": (_i, [C.POINTER(C.c_uint), _i]),

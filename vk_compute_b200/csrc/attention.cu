@@ -81,6 +81,7 @@ struct AttnParams {
     float scale_log2;   // scale * log2(e)
     int pitch;          // floats per partial record, hd + 4 (a multiple of 4)
     int smem;           // dynamic shared memory of the launch (bytes)
+    int stable;         // tokens [0, stable) are written by no kernel still in flight
 };
 
 // One ring stage in 16-byte units: K sub-tile [tt][chunks], then the V
@@ -830,7 +831,6 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
     uint4* qf = reinterpret_cast<uint4*>(smem + Geo::ring_bytes);  // [KS][32]
 
     pdl_launch_dependents();
-    pdl_wait();
 
     // Copy plan: K chunk tid % CH of tokens tid / CH + i (128 / CH); V token
     // tid % TT of chunks tid / TT + i (128 / TT); i < CPT.
@@ -859,8 +859,17 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
             cp_async16_zfill(base + (v_dst0 + i * (kFaThreads / TT) * VROW) * 16, src, vok);
         }
     };
-#pragma unroll
-    for (int s = 0; s < kAttStages; ++s) {
+    // Sub-tiles whose tokens all lie below p.stable (cache rows no kernel still
+    // in flight writes) are requested before the wait on the previous kernel;
+    // the rest, and q, after it.  Commit groups stay in sub-tile order.
+    int s_pre = 0;
+    while (s_pre < kAttStages && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable) {
+        issue(s_pre);
+        cp_commit();
+        ++s_pre;
+    }
+    pdl_wait();
+    for (int s = s_pre; s < kAttStages; ++s) {
         if (s < nsub) issue(s);
         cp_commit();
     }
@@ -1183,7 +1192,7 @@ size_t attention_workspace_bytes(int n_q, int n_kv, int hd, int ctx) {
 
 int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, float* out,
                      int n_q, int n_kv, int hd, int ctx, int ctx_cap, float scale, void* ws, size_t ws_bytes,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int stable = 0) {
     if (!q || !kc || !vc || !out) return set_error(kErrArg, "null attention pointer");
     if (q_bits != 16 && q_bits != 32) return set_error(kErrArg, "q_bits=%d (expected 16 or 32)", q_bits);
     if (n_q <= 0 || n_kv <= 0 || n_q % n_kv != 0)
@@ -1223,6 +1232,7 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     p.tt = attention_subtile(hd);
     p.scale_log2 = scale * kLog2e;
     p.pitch = hd + 4;
+    p.stable = stable;
     // scratch of the final merge: staged records (when they fit) or (m, l), weights and group sums
     const size_t merge_min = ((static_cast<size_t>(G) * pl.records * 12 + 15) & ~size_t(15)) + kAttThreads * 16;
     cudaLaunchConfig_t cfg = {};
@@ -1316,6 +1326,18 @@ int vkc_attention_decode_cache(const void* q, int q_bits, const void* kcache, co
     }
     return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, ctx_cap, scale, workspace,
                             workspace_bytes, s);
+}
+
+// Decode step after an append: the kernel launched just before this one (the
+// fused QKV projection) wrote only token ctx - 1 of the caches, and tokens
+// [0, ctx - 1) come from earlier steps, so they are requested before the wait
+// on that kernel.
+int vkc_attention_decode_append(const void* q, int q_bits, const void* kcache, const void* vcache, float* out,
+                                int n_q, int n_kv, int head_dim, int ctx, int ctx_cap, float scale, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!workspace) return set_error(kErrArg, "attention workspace missing");
+    return attention_launch(q, q_bits, kcache, vcache, out, n_q, n_kv, head_dim, ctx, ctx_cap, scale, workspace,
+                            workspace_bytes, static_cast<cudaStream_t>(stream), ctx - 1);
 }
 
 // ---------------------------------------------------------------------------

@@ -271,7 +271,7 @@ class ShardedDecoder:
                                 kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv,
                                 peer=peer_in)
             ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
-                                 workspace=b.ws, out=b.attn, ctx_cap=cfg.ctx)
+                                 workspace=b.ws, out=b.attn, ctx_cap=cfg.ctx, after_append=True)
             if single:
                 ops.gemv_residual(L.o, b.attn, b.x, out=b.x_mid)
                 ops.rmsnorm_swiglu(L.gate, L.up, b.x_mid, L.g_ffn, eps=cfg.eps, out=b.h)

@@ -236,14 +236,18 @@ def attention_workspace(n_q: int, n_kv: int, head_dim: int, ctx: int, device="cu
 
 def attention_decode(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx: int,
                      scale: float, workspace: torch.Tensor | None = None, out=None,
-                     stream=None, ctx_cap: int | None = None) -> torch.Tensor:
+                     stream=None, ctx_cap: int | None = None, after_append: bool = False) -> torch.Tensor:
     """q [n_q*hd] fp16 or fp32; kcache fp16 [cap][n_kv][hd];
     vcache fp16 [n_kv][hd/8][cap][8] with cap = ctx_cap (default ctx);
-    attends tokens [0, ctx)."""
+    attends tokens [0, ctx).  after_append: the previous kernel wrote only
+    token ctx - 1 of the caches (vkc_attention_decode_append)."""
     o = _out(n_q * head_dim, q, out)
     qb = 32 if q.dtype == torch.float32 else 16
     ws_n = 0 if workspace is None else workspace.numel()
-    if ctx_cap is None:
+    if after_append:
+        check(lib().vkc_attention_decode_append(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
+                                                ctx_cap or ctx, scale, _p(workspace), ws_n, _s(stream)))
+    elif ctx_cap is None:
         check(lib().vkc_attention_decode(_p(q), qb, _p(kcache), _p(vcache), _p(o), n_q, n_kv, head_dim, ctx,
                                          scale, _p(workspace), ws_n, _s(stream)))
     else:
@@ -284,6 +288,10 @@ def gemm_bf16_status(clear: bool = True) -> int:
 
 def set_pdl(enable: bool) -> None:
     lib().vkc_set_pdl(int(enable))
+
+
+def get_pdl() -> bool:
+    return bool(lib().vkc_get_pdl())
 
 
 def device_status(clear: bool = False) -> int:
