@@ -53,3 +53,14 @@ def test_operator_registered(shader):
 
 def test_unknown_operator():
     assert lib().vkc_has_operator(b"RmsNorm-QKV-score-V.spv") == 0
+
+
+def test_peer_input_layout_matches_header():
+    """ops.PeerInput mirrors vkc_peer_input (two pointers, then rank and world)."""
+    import ctypes as C
+
+    from vk_compute_b200.ops import PeerInput
+
+    assert C.sizeof(PeerInput) == 2 * C.sizeof(C.c_void_p) + 2 * C.sizeof(C.c_int)
+    assert [f[0] for f in PeerInput._fields_] == ["slots", "save", "rank", "world"]
+    assert PeerInput.rank.offset == 2 * C.sizeof(C.c_void_p)
