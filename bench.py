@@ -18,9 +18,10 @@ total over ranks, timed as the max over ranks.
 
 The line also carries `decode_step`: one token through the 36-layer int4
 decoder chain (QKV+RoPE+KV append, GQA attention over 8192 cached tokens, O,
-RmsNorm-SwiGLU, down), row/head-sharded over the N GPUs with NCCL
-all-gathers, as device us per step (max over ranks) -- the decode-step
-latency at 1/2/4/8 GPUs.
+RmsNorm-SwiGLU, down), sharded over the N GPUs by heads and by the O / down
+projections' inputs with two NVLink exchanges per layer fused into the
+kernels, as device us per step (max over ranks) -- the decode-step latency at
+1/2/4/8 GPUs.
 
 --impl reference times the reference's CPU algorithm (the oracle's C port of
 src/compute.c's loops over the src/data.c storage, all host threads) on the
