@@ -549,6 +549,64 @@ __device__ __forceinline__ void decode_pairs(const uint4 c, uint64_t (&w)[64 / B
     }
 }
 
+// Cluster reduce-scatter epilogue of the batched kernels.  colsum(m, c) is
+// this CTA's partial sum for vector m and column c (c < C), scal(i) its i-th
+// scalar (i < 2 MS: the sum of squares and the zero-point constant of each
+// vector).  Rank d finalises columns [d share, (d + 1) share): every rank
+// stores its partials for those columns and its scalars into slot `rank` of
+// rank d's receive buffer rbuf [S][MS share + 2 MS] over DSMEM, arrives on
+// d's barrier (initialised for S - 1 arrivals), and each rank adds the S
+// slots in rank order (deterministic) and writes y.
+template <int MS, bool NORM, bool QUANT, typename ColSum, typename Scal>
+__device__ __forceinline__ void batched_reduce_scatter(const BatchParams& p, float* rbuf, uint64_t* red_bar, int S,
+                                                       int rank, int C, int col0, int M, ColSum colsum, Scal scal) {
+    const int tid = threadIdx.x;
+    if (S > 1) cluster_wait_acquire();  // every rank's barrier is initialised
+    const int share = (C + S - 1) / S;
+    const int rstride = MS * share + 2 * MS;
+    const uint32_t my_slot = smem_addr(rbuf) + static_cast<uint32_t>(rank * rstride * 4);
+    if (tid < C) {
+        const int dest = tid / share, cl = tid % share;
+        const uint32_t dst = dest == rank ? my_slot : map_cluster_addr(my_slot, dest);
+        for (int m = 0; m < M; ++m) {
+            const float v = colsum(m, tid);
+            if (dest == rank) rbuf[rank * rstride + m * share + cl] = v;
+            else st_cluster_f32(dst + 4u * (m * share + cl), v);
+        }
+    }
+    if (tid < 2 * MS) {
+        const float v = scal(tid);
+        for (int d = 0; d < S; ++d) {
+            if (d == rank) rbuf[rank * rstride + MS * share + tid] = v;
+            else st_cluster_f32(map_cluster_addr(my_slot, d) + 4u * (MS * share + tid), v);
+        }
+    }
+    __syncthreads();
+    if (S > 1 && tid == 0) {
+        fence_acq_rel_cluster();
+        for (int d = 0; d < S; ++d)
+            if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(red_bar), d));
+        bool ok = false;
+        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(red_bar), 0);
+        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
+    }
+    __syncthreads();
+    const int cc = rank * share + tid;
+    if (tid < share && cc < C && col0 + cc < p.N) {
+        for (int m = 0; m < M; ++m) {
+            float a = 0.f, sq = 0.f, zc = 0.f;
+            for (int q = 0; q < S; ++q) {
+                const float* rp = rbuf + q * rstride;
+                a += rp[m * share + tid];
+                sq += rp[MS * share + 2 * m];
+                zc += rp[MS * share + 2 * m + 1];
+            }
+            const float inv = NORM ? 1.0f / sqrtf(sq * p.inv_dim + p.eps) : 1.0f;
+            p.y[static_cast<size_t>(m) * p.N + col0 + cc] = (QUANT ? a - zc : a) * inv;
+        }
+    }
+}
+
 template <int BITS, int M, bool NORM>
 __global__ void __launch_bounds__(kThreads, 2) gemv_batched_kernel(const BatchParams p) {
     constexpr int KPC = 128 / BITS, NP = KPC / 2;
@@ -660,59 +718,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_kernel(const BatchPa
     }
     __syncthreads();
 
-    // cluster reduce-scatter: rank d finalises columns [d*share, (d+1)*share);
-    // every rank stores its partials for those columns, and its 2M scalars,
-    // into slot `rank` of rank d's receive buffer [S][M*share + 2M], then
-    // arrives on d's barrier; each rank adds the S slots in rank order.
-    if (S > 1) cluster_wait_acquire();  // every rank's barrier is initialised
-    const int share = (C + S - 1) / S;
-    const int rstride = M * share + 2 * M;
-    const uint32_t my_slot = smem_addr(rbuf) + static_cast<uint32_t>(rank * rstride * 4);
-    if (tid < C) {
-        const int dest = tid / share, cl = tid % share;
-        const uint32_t dst = dest == rank ? my_slot : map_cluster_addr(my_slot, dest);
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
+    batched_reduce_scatter<M, NORM, kQuant>(
+        p, rbuf, &red_bar, S, rank, C, col0, M,
+        [&](int m, int c) {
             float v = 0.f;
-            for (int g = 0; g < G; ++g) v += red[m][g * C + tid];
-            if (dest == rank) rbuf[rank * rstride + m * share + cl] = v;
-            else st_cluster_f32(dst + 4u * (m * share + cl), v);
-        }
-    }
-    if (tid < 2 * M) {
-        float v = 0.f;
+            for (int g = 0; g < G; ++g) v += red[m][g * C + c];
+            return v;
+        },
+        [&](int i) {
+            float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) v += wred[w][tid];
-        for (int d = 0; d < S; ++d) {
-            if (d == rank) rbuf[rank * rstride + M * share + tid] = v;
-            else st_cluster_f32(map_cluster_addr(my_slot, d) + 4u * (M * share + tid), v);
-        }
-    }
-    __syncthreads();
-    if (S > 1 && tid == 0) {
-        fence_acq_rel_cluster();
-        for (int d = 0; d < S; ++d)
-            if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(&red_bar), d));
-        bool ok = false;
-        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
-        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
-    }
-    __syncthreads();
-    const int cc = rank * share + tid;
-    if (tid < share && cc < C && col0 + cc < p.N) {
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            float a = 0.f, sq = 0.f, zc = 0.f;
-            for (int q = 0; q < S; ++q) {
-                const float* rp = rbuf + q * rstride;
-                a += rp[m * share + tid];
-                sq += rp[M * share + 2 * m];
-                zc += rp[M * share + 2 * m + 1];
-            }
-            const float inv = NORM ? 1.0f / sqrtf(sq * p.inv_dim + p.eps) : 1.0f;
-            p.y[static_cast<size_t>(m) * p.N + col0 + cc] = (kQuant ? a - zc : a) * inv;
-        }
-    }
+            for (int w = 0; w < kThreads / 32; ++w) v += wred[w][i];
+            return v;
+        });
 }
 
 // ---- Batched decode on the tensor cores (int8 / int4 weights) ------------
@@ -980,54 +998,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_mma_kernel(const Bat
     }
     __syncthreads();
 
-    // cluster reduce-scatter (as gemv_batched_kernel)
-    if (S > 1) cluster_wait_acquire();
-    const int share = (C + S - 1) / S;
-    const int rstride = kMaxBatch * share + 2 * kMaxBatch;
-    const uint32_t my_slot = smem_addr(rbuf) + static_cast<uint32_t>(rank * rstride * 4);
-    if (tid < C) {
-        const int dest = tid / share, cl = tid % share;
-        const uint32_t dst = dest == rank ? my_slot : map_cluster_addr(my_slot, dest);
-        for (int m = 0; m < M; ++m) {
+    batched_reduce_scatter<kMaxBatch, NORM, true>(
+        p, rbuf, &red_bar, S, rank, C, col0, M,
+        [&](int m, int c) {
             float v = 0.f;
-            for (int q = 0; q < RG; ++q) v += red[(q * 8 + m) * C + tid];
-            if (dest == rank) rbuf[rank * rstride + m * share + cl] = v;
-            else st_cluster_f32(dst + 4u * (m * share + cl), v);
-        }
-    }
-    if (tid < 2 * kMaxBatch) {
-        float v = 0.f;
+            for (int q = 0; q < RG; ++q) v += red[(q * 8 + m) * C + c];
+            return v;
+        },
+        [&](int i) {
+            float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) v += wred[w][tid];
-        for (int d = 0; d < S; ++d) {
-            if (d == rank) rbuf[rank * rstride + kMaxBatch * share + tid] = v;
-            else st_cluster_f32(map_cluster_addr(my_slot, d) + 4u * (kMaxBatch * share + tid), v);
-        }
-    }
-    __syncthreads();
-    if (S > 1 && tid == 0) {
-        fence_acq_rel_cluster();
-        for (int d = 0; d < S; ++d)
-            if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(&red_bar), d));
-        bool ok = false;
-        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
-        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
-    }
-    __syncthreads();
-    const int cc = rank * share + tid;
-    if (tid < share && cc < C && col0 + cc < p.N) {
-        for (int m = 0; m < M; ++m) {
-            float a = 0.f, sq = 0.f, zc = 0.f;
-            for (int q = 0; q < S; ++q) {
-                const float* rp = rbuf + q * rstride;
-                a += rp[m * share + tid];
-                sq += rp[kMaxBatch * share + 2 * m];
-                zc += rp[kMaxBatch * share + 2 * m + 1];
-            }
-            const float inv = NORM ? 1.0f / sqrtf(sq * p.inv_dim + p.eps) : 1.0f;
-            p.y[static_cast<size_t>(m) * p.N + col0 + cc] = (a - zc) * inv;
-        }
-    }
+            for (int w = 0; w < kThreads / 32; ++w) v += wred[w][i];
+            return v;
+        });
 }
 
 struct DeviceInfo {
