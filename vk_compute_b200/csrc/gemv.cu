@@ -467,6 +467,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
         return;
     }
     if (S > 1) {
+        // This bound (kSpinLimit suspending try-waits: seconds) is far longer
+        // than any wait the other ranks can be held in before they deposit
+        // (their own bounded waits: 100 ms for a peer exchange), so rank 0
+        // does not give up and exit while a deposit into its shared memory
+        // is still to come.
         if (tid == 0) {
             bool ok = false;
             for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
