@@ -54,11 +54,20 @@ void vkc_set_timing(int enable);
 int vkc_get_timing(void);
 /* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
 int vkc_has_operator(const char* shader);
-/* Waits for the current device and returns its status word: bit 0 set when a
- * kernel's producer warp, bit 1 when a consumer warp, gave up a bounded
- * wait (the kernel then ends early and its outputs are invalid).  `clear`
- * resets the word.  No counterpart in the reference. */
+/* Waits for the current device and returns its status word, whose flags
+ * record a bounded device wait that gave up (the kernel then ends early and
+ * its outputs are invalid): 0x1 a producer warp, 0x2 a consumer warp, 0x4 a
+ * cluster's collecting CTA (split-K deposits), 0x8 a wait for another GPU's
+ * data (peer timeout).  `clear` resets the word.  No counterpart in the
+ * reference. */
 int vkc_device_status(unsigned* status, int clear);
+/* Bounds of those waits, in nanoseconds of the GPU clock: `peer_ns`, the
+ * longest one thread waits in total for other GPUs' data in a fused exchange
+ * (one deadline, started at its first wait); `cluster_ns`, the longest a
+ * cluster's collecting CTA waits for the other CTAs' deposits into its shared
+ * memory (at least ten times peer_ns, so it outlasts every wait that can hold
+ * a depositing CTA back).  No counterpart in the reference. */
+void vkc_wait_limits(uint64_t* peer_ns, uint64_t* cluster_ns);
 
 /* y = W^T x.  Replaces shader/GEMV-FP16.comp, GEMV-INT8.comp, GEMV-INT4.comp
  * and gemv.comp (fp32), bindings {x, W, y[, s, z]}. */
@@ -127,8 +136,8 @@ int vkc_rmsnorm_swiglu(int bits, const void* wg, const float* sg, const float* z
  * `slots` ([world][K] words in this rank's memory, 8-byte aligned) summed in
  * rank order; the previous launch on the stream must be this rank's
  * vkc_gemv_peer into the same buffer.  x is also stored to `save` (K floats)
- * unless NULL.  A thread that has waited 100 ms in total sets bit 8 of the
- * device status word (vkc_device_status) and stops waiting. */
+ * unless NULL.  A thread whose waits reach 100 ms in total sets flag 0x8 of
+ * the device status word (vkc_device_status) and stops waiting. */
 typedef struct vkc_peer_input {
     const void* slots;
     float* save;
@@ -206,8 +215,10 @@ int vkc_attention_decode_append(const void* q, int q_bits, const void* kcache, c
  * vkc_attention_decode, but its scratch is a fixed 2 MiB array inside the
  * library (held by every GPU that loads the library until it is unloaded);
  * shapes needing more (vkc_attention_workspace_bytes) are rejected with
- * VKC_ERR_ARG.  The first call on a device looks up the array's address and
- * clears its tickets, so make that first call before any stream capture.  All
+ * VKC_ERR_ARG.  Every call looks up the array's address in the current
+ * context; the first call on a device (and the first in a new context) also
+ * clears its tickets with a memset on `stream`, so make that first call before
+ * any stream capture.  All
  * calls share the array: calls that overlap on the GPU (different streams)
  * race; calls ordered on one stream do not. */
 size_t vkc_attention_noalloc_max_scratch(void);
@@ -227,7 +238,7 @@ int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, 
  * (world unsigned each, zero before the first launch), all mapped into this
  * process (CUDA IPC).  Every rank makes the same sequence of launches; a launch
  * returns on the GPU once every rank's slice has arrived here.  A wait that
- * exceeds its bound sets bit 8 in *status (device memory) instead of hanging. */
+ * exceeds its bound sets flag 0x8 in *status (device memory) instead of hanging. */
 int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats,
                       int rank, int world, unsigned* status, void* stream);
 /* All-reduce with residual for K-split projections (no counterpart in the
@@ -252,8 +263,8 @@ int vkc_ipc_free(void* ptr);
  * contraction (shader/gemm.comp:19-59) for prefill.  K a multiple of 64, N a
  * multiple of 96, any M (tiles of 128 rows).  Pointers 16-byte aligned. */
 int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, void* stream);
-/* Status bits of vkc_gemm_bf16 on the current device (16: a bounded wait ran
- * out); waits for the device; `clear` resets them. */
+/* Status flags of vkc_gemm_bf16 on the current device (0x10: a bounded wait
+ * ran out); waits for the device; `clear` resets them. */
 int vkc_gemm_bf16_status(unsigned* status, int clear);
 
 /* ---- weight preparation on the GPU (bit-identical to src/data.c) ---- */

@@ -255,7 +255,7 @@ static inline uint32_t code_at(const uint8_t* data, int bits, int K, int N, int 
 }
 
 /* Dense weight: w = q * s - z with s, z of block c/256, as the shaders do it
- * (shader/GEMV-INT8.comp:107, GEMV-INT4.comp:179) and as the reference CPU
+ * (shader/GEMV-INT8.comp:56-59, GEMV-INT4.comp:57-64) and as the reference CPU
  * check writes it (src/compute.c:248,263). */
 void vko_dequant(const uint8_t* data, const float* scale, const float* zero, int K, int N,
                  int bits, float* w) {

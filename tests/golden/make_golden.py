@@ -7,6 +7,9 @@ SHA-256 digests).  The fixtures pin the oracle and the product's data
 functions bit-for-bit to the reference.
 
     bash oracle/build_ref.sh && python tests/golden/make_golden.py
+
+It also runs src/compute.c's own CPU check loops (oracle/_ref/libvkref_loops.so)
+and stores their results, which pin the oracle's operator arithmetic.
 """
 from __future__ import annotations
 
@@ -18,6 +21,16 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
 REF = ROOT / "oracle" / "_ref" / "libvkref_data.so"
+REF_LOOPS = ROOT / "oracle" / "_ref" / "libvkref_loops.so"
+
+# src/compute.c's own CPU check loops (oracle/ref_loops.c around the line
+# ranges oracle/build_ref.sh extracts), on compute.c's inputs: x seed 4321,
+# gamma 58923, weights 936 (src/compute.c:18-20, 28, 32).  Shapes: compute.c's
+# own K=4096, N=12288, and a small one.  The quantised loops read the first
+# scale block and INT4's high nibble, so indices are even and below 256.
+LOOP_OPS = ("gemv_f32", "rmsnorm_gemv_f32", "swiglu_f32", "gemv_int8", "gemv_int4", "swiglu_int8", "swiglu_int4")
+LOOP_SHAPES = ((4096, 12288), (1024, 512))
+LOOP_IDX = np.array([0, 2, 10, 64, 128, 200, 254], np.int32)
 OUT = Path(__file__).resolve().parent / "reference_data.npz"
 
 
@@ -117,6 +130,19 @@ def main() -> None:
     g["pack16"] = pack(h16, 32, 256, 16)
     g["pack8"] = pack(g["q8_936_data"], 32, 512, 8)
     g["pack4"] = pack(g["q4_936_data"], 64, 512, 4)
+
+    loops = C.CDLL(str(REF_LOOPS))
+    g["refloop_idx"] = LOOP_IDX
+    g["refloop_seeds"] = np.array([4321, 58923, 936], np.int32)
+    for K, N in LOOP_SHAPES:
+        for op in LOOP_OPS:
+            fn = getattr(loops, f"vkref_{op}")
+            fn.restype = None
+            fn.argtypes = [C.c_int] * 5 + [C.c_void_p, C.c_int, C.c_void_p]
+            out = np.zeros(len(LOOP_IDX), np.float32)
+            fn(K, N, 4321, 58923, 936, LOOP_IDX.ctypes.data_as(C.c_void_p), len(LOOP_IDX),
+               out.ctypes.data_as(C.c_void_p))
+            g[f"refloop_{op}_{K}x{N}"] = out
 
     np.savez_compressed(OUT, **g)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")

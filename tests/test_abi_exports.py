@@ -55,6 +55,20 @@ def test_unknown_operator():
     assert lib().vkc_has_operator(b"RmsNorm-QKV-score-V.spv") == 0
 
 
+def test_wait_limits_outlast_each_other():
+    """The collecting CTA of a split-K cluster waits (on the GPU clock) at
+    least ten times as long as any peer wait that can hold a depositing CTA
+    back, so it never exits while a deposit into its shared memory is still
+    to come; both are finite, so no device wait is unbounded."""
+    import ctypes as C
+
+    peer, cluster = C.c_uint64(), C.c_uint64()
+    lib().vkc_wait_limits(C.byref(peer), C.byref(cluster))
+    assert 0 < peer.value <= 1_000_000_000
+    assert cluster.value >= 10 * peer.value
+    assert cluster.value <= 10_000_000_000
+
+
 def test_peer_input_layout_matches_header():
     """ops.PeerInput mirrors vkc_peer_input (two pointers, then rank and world)."""
     import ctypes as C

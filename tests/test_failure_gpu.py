@@ -1,7 +1,9 @@
 """Failure detection without a GPU fault: a fused exchange consumer whose peer
 never delivers (its slot words keep an old flag: nothing writes them) gives up
-after its bounded wait (100 ms per thread), records bit 8 in the device status
-word and returns; the device stays usable and later results are correct."""
+once its wait reaches the bound (one 100 ms deadline per thread, started at
+the thread's first wait and shared by all the elements it waits for), records
+status flag 0x8 (peer timeout) in the device status word and returns; the
+device stays usable and later results are correct."""
 import struct
 
 import numpy as np

@@ -8,7 +8,11 @@ the library.  Two calls in a row through the C ABI must match the ordinary
 entry point (vkc_attention_decode with a caller workspace); the second call
 also checks that the merge tickets the first call left behind are clean.
 
-This file is collected last on purpose; it runs alone or after the others.
+The file name makes pytest collect it last, so that a run stopped at its
+first failure has already run every other test if this one fails.  It
+depends on no state the other tests leave: it passes alone in a fresh process
+and after them, because each call looks up the array in the current context
+and leaves the tickets at zero.
 """
 import ctypes as C
 import math

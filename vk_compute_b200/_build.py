@@ -25,7 +25,6 @@ LIB = PKG / "libvkcompute.so"
 E2E_BIN = PKG / "vkc_e2e_bench"
 ORACLE = ROOT / "oracle"
 ORACLE_LIB = ORACLE / "liboracle.so"
-REFERENCE = Path(os.environ.get("VKC_REFERENCE", "/root/reference"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
@@ -100,12 +99,15 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def build_reference(force: bool = False) -> bool:
-    """Compile the reference's own C sources into oracle/_ref (checker only)."""
-    if not (REFERENCE / "src" / "data.c").exists():
-        return False
+    """Compile the reference's own C sources into oracle/_ref (checker only).
+    oracle/build_ref.sh locates the sources (VKC_REFERENCE, or where they are
+    mounted) and exits 3 when they are absent, as on a machine that only runs
+    the prebuilt files."""
     script = ORACLE / "build_ref.sh"
-    env = dict(os.environ, VKC_REFERENCE=str(REFERENCE), VKC_FORCE="1" if force else "0")
+    env = dict(os.environ, VKC_FORCE="1" if force else "0")
     proc = subprocess.run(["bash", str(script)], capture_output=True, text=True, env=env)
+    if proc.returncode == 3:
+        return False
     if proc.returncode != 0:
         sys.stderr.write(proc.stdout + proc.stderr)
         raise RuntimeError("reference build recipe failed")

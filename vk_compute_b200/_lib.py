@@ -24,6 +24,7 @@ SIGNATURES = {
     "vkc_get_timing": (_i, []),
     "vkc_has_operator": (_i, [C.c_char_p]),
     "vkc_device_status": (_i, [C.POINTER(C.c_uint), _i]),
+    "vkc_wait_limits": (None, [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),
     "vkc_rmsnorm_gemv": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
     "vkc_rmsnorm_gemv_rope": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p]),

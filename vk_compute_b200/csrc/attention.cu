@@ -1362,24 +1362,27 @@ constexpr size_t kNoAllocScratchBytes = 2u << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch per device
+void* g_noalloc_addr[64] = {};  // last address of g_noalloc_scratch seen per device
 
-// Once per device, with that device current: look up the array's device
-// address (in host code its name is only a stand-in) and clear the tickets.
+// On every call, with the calling device current: look up the array's device
+// address in the current context (in host code its name is only a stand-in,
+// and a context made after cudaDeviceReset, or by a plugin host, loads its own
+// copy of the array).  When the address differs from the one this device had
+// last time (the first call, or another context's copy), clear the tickets.
 int noalloc_scratch(void** out, cudaStream_t stream) {
     int dev = 0;
     VKC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+        return set_error(kErrCuda, "cudaGetSymbolAddress(attention scratch) failed: %s", cudaGetErrorString(e));
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess)
-            return set_error(kErrCuda, "cudaGetSymbolAddress(attention scratch) failed: %s", cudaGetErrorString(e));
+    if (g_noalloc_addr[dev] != p) {
         VKC_CUDA_TRY(cudaMemsetAsync(p, 0, kWorkspaceHeader, stream));
         g_noalloc_addr[dev] = p;
     }
-    *out = g_noalloc_addr[dev];
+    *out = p;
     return kOk;
 }
 }  // namespace

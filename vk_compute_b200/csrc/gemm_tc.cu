@@ -18,7 +18,7 @@
 //   to the producer with tcgen05.commit on the stage's "empty" mbarrier.
 // - After the last tile a commit signals the epilogue: the four warps read
 //   their 32 TMEM lanes (rows) with tcgen05.ld and store fp32 rows of C.
-// Every mbarrier wait is bounded; a timeout sets bit 16 of the status word and
+// Every mbarrier wait is bounded; a timeout sets flag 0x10 of the status word and
 // the kernel stops issuing work, waits for its copies, frees TMEM and returns.
 #include "vkc_common.cuh"
 
@@ -306,7 +306,7 @@ int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, v
     return kOk;
 }
 
-// Status bits of the tensor-core GEMM on the current device (bit 16: a bounded
+// Status flags of the tensor-core GEMM on the current device (0x10: a bounded
 // wait ran out); reading waits for the device, `clear` resets.
 int vkc_gemm_bf16_status(unsigned* out, int clear) {
     VKC_CUDA_TRY(cudaDeviceSynchronize());

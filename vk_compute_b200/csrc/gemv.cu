@@ -7,7 +7,7 @@
 // chunk at byte (r*N + j)*16, so a chunk row is a contiguous N*16-byte stream.
 // Quantised weights carry fp32 scale s and zero z per (k, 256-output block b),
 // block-major at b*K + k (src/data.c:122-124), dequantised as q*s - z
-// (shader/GEMV-INT8.comp:107).
+// (shader/GEMV-INT8.comp:56-59).
 //
 // Decomposition.  A CTA of 256 threads owns C consecutive outputs
 // (C in {256, 128, 64, 32}, inside one scale block) and a range of chunk rows;
@@ -315,7 +315,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
             }
         }
     };
-    bool gave_up = false;  // a peer wait ran out (100 ms): later elements do not wait again
+    // One deadline per thread for all its peer waits (kPeerWaitNs after its
+    // first wait); once it has passed, later elements do not wait again.
+    uint64_t deadline = 0;
+    bool gave_up = false;
     auto load_x = [&](int base) {
 #pragma unroll
         for (int q = 0; q < kMaxAct; ++q) {
@@ -328,9 +331,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
                     const unsigned long long* src = p.xslots + static_cast<size_t>(w) * p.K + k;
                     unsigned long long word = ld_relaxed_sys_u64(src);
                     if (static_cast<unsigned>(word >> 32) != flag && !gave_up) {
-                        const uint64_t t0 = globaltimer_ns();
+                        if (deadline == 0) deadline = globaltimer_ns() + kPeerWaitNs;
                         while (static_cast<unsigned>((word = ld_relaxed_sys_u64(src)) >> 32) != flag) {
-                            if (globaltimer_ns() - t0 > kPeerWaitNs) {  // bounded: give up, flag it
+                            if (globaltimer_ns() > deadline) {  // bounded: give up, flag it
                                 atomicOr(&g_status, kStatusPeerTimeout);
                                 gave_up = true;
                                 break;
@@ -467,16 +470,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
         return;
     }
     if (S > 1) {
-        // This bound (kSpinLimit suspending try-waits: seconds) is far longer
-        // than any wait the other ranks can be held in before they deposit
-        // (their own bounded waits: 100 ms for a peer exchange), so rank 0
-        // does not give up and exit while a deposit into its shared memory
-        // is still to come.
-        if (tid == 0) {
-            bool ok = false;
-            for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(&red_bar), 0);
-            if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
-        }
+        // kClusterWaitNs (1 s on the clock) is ten times the longest the other
+        // ranks can be held before they deposit (each thread's peer waits
+        // total at most kPeerWaitNs), so rank 0 does not give up and exit
+        // while a deposit into its shared memory is still to come.
+        if (tid == 0 && !mbar_wait_cluster_ns(smem_addr(&red_bar), 0, kClusterWaitNs))
+            atomicOr(&g_status, kStatusReduceTimeout);
     }
     __syncthreads();
     if (tid < C || warp == 0) {
@@ -591,9 +590,9 @@ __device__ __forceinline__ void batched_reduce_scatter(const BatchParams& p, flo
         fence_acq_rel_cluster();
         for (int d = 0; d < S; ++d)
             if (d != rank) mbar_arrive_remote(map_cluster_addr(smem_addr(red_bar), d));
-        bool ok = false;
-        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait_cluster(smem_addr(red_bar), 0);
-        if (!ok) atomicOr(&g_status, kStatusReduceTimeout);
+        // the other ranks arrive once their weight streams end (no peer waits
+        // in the batched kernels): kClusterWaitNs on the clock is far beyond that
+        if (!mbar_wait_cluster_ns(smem_addr(red_bar), 0, kClusterWaitNs)) atomicOr(&g_status, kStatusReduceTimeout);
     }
     __syncthreads();
     const int cc = rank * share + tid;
@@ -1559,6 +1558,11 @@ int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const 
 
 // Status word of the current device (bits: kStatus*).  Reading waits for the
 // device; `clear` resets it.
+void vkc_wait_limits(uint64_t* peer_ns, uint64_t* cluster_ns) {
+    if (peer_ns) *peer_ns = kPeerWaitNs;
+    if (cluster_ns) *cluster_ns = kClusterWaitNs;
+}
+
 int vkc_device_status(unsigned* status, int clear) {
     VKC_CUDA_TRY(cudaDeviceSynchronize());
     uint32_t v = 0;

@@ -206,7 +206,7 @@ struct OpInfo {
 
 // Bindings per operator (shader layout(binding = i) declarations):
 //   GEMV-*            {x, W, y [, s, z]}             shader/GEMV-INT8.comp:14-16,68-69
-//   RmsNorm-GEMV-*    {x, gamma, W, y [, s, z]}      shader/RmsNorm-GEMV-INT8.comp:93-98
+//   RmsNorm-GEMV-*    {x, gamma, W, y [, s, z]}      shader/RmsNorm-GEMV-INT8.comp:20-25
 //   RmsNorm-GEMV-Rope {x, gamma, W, y, theta}        shader/RmsNorm-GEMV-Rope-FP16.comp:21-25
 //                     {x, gamma, W, y, s, z, theta}  shader/RmsNorm-GEMV-Rope-INT4.comp
 //   swiglu            {x, gamma, G, U, y [, sG, zG, sU, zU]}  shader/RmsNorm-swiglu-ffn-INT4.comp:20-28

@@ -219,8 +219,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Longest a thread waits, in total, for other GPUs' data in a fused exchange.
+// Longest a thread waits, in total, for other GPUs' data in a fused exchange:
+// one deadline per thread, started at its first wait and shared by every
+// element it waits for afterwards.
 constexpr uint64_t kPeerWaitNs = 100ull * 1000 * 1000;
+// Longest a cluster's collecting CTA waits for the other CTAs' deposits into
+// its shared memory.  A depositing CTA can be held before its deposit only by
+// its own peer waits (kPeerWaitNs in total per thread) and by its weight
+// stream, so ten times the peer limit leaves the collecting CTA waiting well
+// after every deposit that can still come: it never exits while another CTA
+// may write into its shared memory.
+constexpr uint64_t kClusterWaitNs = 10 * kPeerWaitNs;
+static_assert(kClusterWaitNs >= 10 * kPeerWaitNs, "cluster wait must outlast every peer wait");
 
 // 8-byte words read and written whole (single-copy atomic), for exchanges
 // that carry a flag beside each value instead of ordering data and flags.
@@ -233,6 +243,15 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+
+// Bounded wait, on the clock, for a phase of a cluster-visible mbarrier.
+__device__ __forceinline__ bool mbar_wait_cluster_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_cluster(bar, parity))
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    return true;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
