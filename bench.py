@@ -83,6 +83,15 @@ def ncu_traffic(workload: str):
     return None if v is None else v.get("bytes_per_launch")
 
 
+def ncu_traffic_table() -> dict:
+    """Per-launch DRAM bytes by kernel name (the `kernels` section of
+    profiles/ncu_traffic.json, keyed like the bench's kernel names)."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return {}
+    return {k: v.get("bytes_per_launch") for k, v in json.loads(p.read_text()).get("kernels", {}).items()}
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling in the background."""
 
@@ -142,10 +151,13 @@ class ClockSampler:
 # Workloads (our implementation)
 # ---------------------------------------------------------------------------
 
-def build_workload(name: str, rank: int, device):
-    """Returns (step_fn(i), bytes_per_step, launches_per_step, dominant(i),
-    dominant_bytes, e2e, meta).  step_fn(i) enqueues step i on the current
-    stream."""
+def build_workload(name: str, rank: int, device, world: int = 1):
+    """Returns a dict: step(i) enqueues step i on the current stream; bytes
+    (algorithmic bytes of one rank's step), job_bytes (of the whole job's
+    step), launches, the dominant kernel (fn, bytes, name), kernels (name, fn,
+    bytes) for per-kernel timing, e2e inputs and meta.  With world > 1 the
+    headline workload is one fixed matrix row-sharded over the ranks plus an
+    NVLink all-gather of y; the others run one copy per rank."""
     import torch
 
     from vk_compute_b200 import ops
@@ -165,6 +177,40 @@ def build_workload(name: str, rank: int, device):
                                 None if w.scale is None else w.scale.clone(),
                                 None if w.zero is None else w.zero.clone())
 
+    if name == "rmsnorm_gemv_int8" and world > 1:
+        # The 12288 x 4096 matrix row-sharded: rank r owns outputs
+        # [r*N/world, (r+1)*N/world) (whole 256-row scale blocks) and computes
+        # its slice of y; the library's NVLink peer all-gather then gives
+        # every rank the whole y (strong scaling: the job is fixed).
+        from vk_compute_b200.p2p import PeerGather
+
+        K, N, bits = 4096, 12288, 8
+        n_loc = N // world
+        x = randn(K)
+        gamma = randn(K, std=0.1, mean=1.0)
+        y_loc = torch.empty(n_loc, device=device)
+        peer = PeerGather({"y": N}, device)
+        wg = torch.Generator(device=device).manual_seed(77)
+        full = torch.randn(K, N, generator=wg, device=device) * 0.02
+        shard = full[:, rank * n_loc:(rank + 1) * n_loc].contiguous()
+        del full
+        wbytes = K * n_loc + 8 * K * n_loc // 256
+        pool = pool_of(lambda j: ops.pack_dense(shard, bits, symmetric=True, fp16_scale=True), wbytes)
+        del shard
+
+        def step(i):
+            ops.rmsnorm_gemv(pool[i % len(pool)], x, gamma, eps=1e-6, out=y_loc)
+            peer.gather("y", y_loc)
+
+        gemv = lambda i: ops.rmsnorm_gemv(pool[i % len(pool)], x, gamma, eps=1e-6, out=y_loc)
+        job = K * N + 8 * K * N // 256 + 4 * K * 2 + 4 * N
+        rank_bytes = wbytes + 4 * K * 2 + 4 * n_loc
+        meta = {"K": K, "N": N, "bits": bits, "rows_per_rank": n_loc, "pool": len(pool),
+                "pool_bytes": len(pool) * wbytes, "exchange": "NVLink peer all-gather of y (vkc_allgather_p2p)"}
+        return dict(step=step, bytes=rank_bytes, job_bytes=job, scaling="strong", launches=2, dominant=gemv,
+                    dominant_bytes=rank_bytes, dominant_name=f"RmsNorm-GEMV-INT8 {n_loc}x{K} shard", meta=meta,
+                    e2e=None, e2e_sharded=(x, peer.buffers["y"], K, N), kernels=[], close=peer.close)
+
     if name in ("rmsnorm_gemv_int8", "gemv_fp16"):
         if name == "rmsnorm_gemv_int8":
             K, N, bits = 4096, 12288, 8
@@ -183,9 +229,10 @@ def build_workload(name: str, rank: int, device):
             act = 4 * K + 4 * N
             step = lambda i: ops.gemv(pool[i % len(pool)], x, out=y)
         meta = {"K": K, "N": N, "bits": bits, "pool": len(pool), "pool_bytes": len(pool) * wbytes}
+        kname = "RmsNorm-GEMV-INT8" if bits == 8 else "GEMV-FP16"
         return dict(step=step, bytes=wbytes + act, launches=1, dominant=step, dominant_bytes=wbytes + act,
-                    dominant_name=("RmsNorm-GEMV-INT8" if bits == 8 else "GEMV-FP16"), meta=meta,
-                    e2e=(pool, x, gamma, y, K, N, bits))
+                    dominant_name=kname, meta=meta, e2e=(pool, x, gamma, y, K, N, bits),
+                    kernels=[(kname, step, wbytes + act)])
 
     if name in ("rmsnorm_gemv_int8_batch4", "gemv_int4_batch8"):
         if name == "rmsnorm_gemv_int8_batch4":
@@ -205,8 +252,9 @@ def build_workload(name: str, rank: int, device):
             act = 4 * M * K + 4 * M * N
             step = lambda i: ops.gemv_batched(pool[i % len(pool)], x, out=y)
         meta = {"K": K, "N": N, "bits": bits, "vectors": M, "pool": len(pool), "pool_bytes": len(pool) * wbytes}
+        kname = f"batched GEMV INT{bits} x{M}"
         return dict(step=step, bytes=wbytes + act, launches=1, dominant=step, dominant_bytes=wbytes + act,
-                    dominant_name=f"batched GEMV INT{bits} x{M}", meta=meta, e2e=None)
+                    dominant_name=kname, meta=meta, e2e=None, kernels=[(kname, step, wbytes + act)])
 
     if name == "swiglu_ffn_int4":
         H, I = 4096, 12288
@@ -232,10 +280,13 @@ def build_workload(name: str, rank: int, device):
             ops.gemv(d, h, out=out)
 
         dom = lambda i: ops.rmsnorm_swiglu(*layers[i % n][:2], x, gamma, eps=1e-6, out=h)
+        down = lambda i: ops.gemv(layers[i % n][2], h, out=out)
         act = 4 * H * 2 + 4 * I + 4 * I + 4 * H
         return dict(step=step, bytes=layer_bytes + act, launches=2, dominant=dom,
                     dominant_bytes=gu_bytes + 4 * H * 2 + 4 * I, dominant_name="RmsNorm-swiglu-ffn-INT4",
-                    meta={"hidden": H, "intermediate": I, "pool": n}, e2e=None)
+                    meta={"hidden": H, "intermediate": I, "pool": n}, e2e=None,
+                    kernels=[("RmsNorm-swiglu-ffn-INT4 gate/up 2x12288x4096", dom, gu_bytes + 4 * H * 2 + 4 * I),
+                             ("GEMV-INT4 down 4096x12288", down, d_bytes + 4 * I + 4 * H)])
 
     if name == "qkv_rope_attn_int4":
         H, NQ, NKV, HD, CTX = 4096, 32, 8, 128, 8192
@@ -269,10 +320,14 @@ def build_workload(name: str, rank: int, device):
 
         dom = lambda i: ops.attention_decode(qkv[:NQ * HD], layers[i % n][1], layers[i % n][2], NQ, NKV, HD, CTX,
                                              1 / math.sqrt(HD), workspace=ws, out=att)
+        qkv_fn = lambda i: ops.rmsnorm_gemv_rope(layers[i % n][0], x, gamma, theta, pos, mode="pairs", head_dim=HD,
+                                                 rot_rows=(NQ + NKV) * HD, eps=1e-6, out=qkv)
         act = 4 * H * 2 + 4 * NQKV + 4 * NQ * HD * 2
         return dict(step=step, bytes=wbytes + kvbytes + act, launches=2, dominant=dom,
                     dominant_bytes=kvbytes + 4 * NQ * HD * 2, dominant_name="Att-full-FP16",
-                    meta={"pool": n, "pos": pos, "ctx": CTX}, e2e=None)
+                    meta={"pool": n, "pos": pos, "ctx": CTX}, e2e=None,
+                    kernels=[("RmsNorm-GEMV-Rope-INT4 QKV 6144x4096", qkv_fn, wbytes + 4 * H * 2 + 4 * NQKV),
+                             ("Att-full-FP16 32q/8kv x 128, ctx 8192", dom, kvbytes + 4 * NQ * HD * 2)])
     if name == "prefill_gemm_bf16":
         M, N, K = 64, 12288, 4096
         a = randn(M, K).to(torch.bfloat16)
@@ -283,10 +338,10 @@ def build_workload(name: str, rank: int, device):
         ws = [base[j] if j < 2 else base[j % 2].clone() for j in range(n)]
         step = lambda i: ops.gemm_bf16(a, ws[i % n], out=c)
         nbytes = wbytes + M * K * 2 + M * N * 4
+        kname = "gemm_tc_kernel (tcgen05, bf16)"
         return dict(step=step, bytes=nbytes, launches=1, dominant=step, dominant_bytes=nbytes,
-                    dominant_name="gemm_tc_kernel (tcgen05, bf16)", meta={"M": M, "N": N, "K": K, "pool": n,
-                                                                          "flop": 2 * M * N * K},
-                    e2e=None)
+                    dominant_name=kname, meta={"M": M, "N": N, "K": K, "pool": n, "flop": 2 * M * N * K},
+                    e2e=None, kernels=[(kname, step, nbytes)])
     raise SystemExit(f"unknown workload {name}; choose from {sorted(WORKLOADS)}")
 
 
@@ -304,6 +359,65 @@ def capture(fn, count, start=0):
         for i in range(count):
             fn(start + i)
     return g
+
+
+def time_launches(fn, steps: int, start: int = 0) -> float:
+    """Device seconds per call of fn(start), ..., fn(start + steps - 1),
+    captured in one CUDA graph that is replayed once untimed (upload and
+    warm-up: `steps` calls) and then timed with CUDA events on the stream."""
+    import torch
+
+    g = capture(fn, steps, start)
+    stream = torch.cuda.current_stream()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / 1e3 / steps
+
+
+# The other configurations of the headline metric, measured in the default run
+# beside the headline (RmsNorm-GEMV INT8 is config 2): key -> workload.
+CONFIG_WORKLOADS = {"1": "gemv_fp16", "3": "swiglu_ffn_int4", "4": "qkv_rope_attn_int4", "5b": "prefill_gemm_bf16"}
+
+
+def measure_configs(rank: int, device, steps: int, peak: float, device_index: int) -> dict:
+    """Each config's step and each of its kernels alone, graph-launched back
+    to back over the same >= 4x L2 weight pools as the workload itself."""
+    import torch
+
+    traffic = ncu_traffic_table()
+    sampler = ClockSampler(device_index)
+    sampler.start()
+    out = {}
+    for key, name in CONFIG_WORKLOADS.items():
+        wl = build_workload(name, rank, device)
+        torch.cuda.synchronize()
+        step_s = time_launches(wl["step"], steps)
+        kernels = {}
+        for kname, fn, nbytes in wl["kernels"]:
+            ks = step_s if len(wl["kernels"]) == 1 else time_launches(fn, steps)
+            entry = {"us": round(ks * 1e6, 3), "GB_s": round(nbytes / ks / 1e9, 1),
+                     "frac": round(nbytes / ks / 1e9 / peak, 4), "algorithmic_bytes": nbytes,
+                     "traffic": traffic.get(kname)}
+            if "flop" in wl["meta"]:
+                entry["tflops"] = round(wl["meta"]["flop"] / ks / 1e12, 1)
+                entry["tensor_frac"] = round(wl["meta"]["flop"] / ks / 1e12 / tensor_peak(), 4)
+            kernels[kname] = entry
+        out[key] = {"workload": name, "description": WORKLOADS[name], "us_per_step": round(step_s * 1e6, 3),
+                    "GB_s": round(wl["bytes"] / step_s / 1e9, 1), "frac": round(wl["bytes"] / step_s / 1e9 / peak, 4),
+                    "bytes_per_step": wl["bytes"], "launches_per_step": wl["launches"], "kernels": kernels}
+        del wl
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    out["clocks"] = sampler.stop()
+    out["method"] = ("graph-launched back to back, steps rotate through weight pools >= 4x L2; a kernel's us is "
+                     "its own graph of the same launches; frac of the measured HBM copy peak")
+    return out
 
 
 def e2e_dropin(args, e2e, device_index):
@@ -366,7 +480,67 @@ def e2e_dropin(args, e2e, device_index):
     return dt, 4 * K, 4 * N
 
 
-def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float):
+def e2e_sharded(args, wl):
+    """The sharded headline end to end through the Python API on every rank:
+    per step, x host->device from pinned memory, the rank's RmsNorm-GEMV
+    shard and the NVLink all-gather, then the whole y device->host; host wall
+    clock.  Every rank makes the same launches (the gather is collective)."""
+    import torch
+
+    x_dev, y_full, K, N = wl["e2e_sharded"]
+    x_host = torch.empty(K, dtype=torch.float32).pin_memory()
+    x_host.copy_(x_dev.cpu())
+    y_host = torch.empty(N, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream()
+    step = wl["step"]
+
+    def one(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        step(i)
+        y_host.copy_(y_full, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(args.warmup + i)
+    dt = (time.perf_counter() - t0) / args.steps
+    return dt, 4 * K, 4 * N
+
+
+def decode_parity(dec, cfg, rank: int, world: int, device, pos: int) -> dict | None:
+    """One eager step of the sharded model from a seeded x, and (on rank 0)
+    the same step of the same model on one GPU; returns rank 0's
+    norm-relative difference.  The shards are whole scale blocks of the
+    unsharded matrices, so the two are the same quantised model and differ
+    only in the order of the cross-rank sums."""
+    import torch
+
+    from vk_compute_b200.decode import ShardedDecoder
+
+    g = torch.Generator(device=device).manual_seed(4242)
+    x0 = torch.randn(cfg.hidden, generator=g, device=device)
+    dec.buf.x.copy_(x0)
+    got = dec.step(pos).clone()
+    torch.cuda.synchronize()
+    timed_out = dec.timed_out()
+    if rank != 0:
+        return None
+    ref_dec = ShardedDecoder(cfg, rank=0, world=1, device=device, seed=7)
+    ref_dec.buf.x.copy_(x0)
+    ref = ref_dec.step(pos).clone()
+    torch.cuda.synchronize()
+    err = float((got - ref).abs().max() / ref.abs().max())
+    del ref_dec
+    torch.cuda.empty_cache()
+    return {"max_rel_err": err, "bar": 5e-3, "ok": bool(err <= 5e-3 and not timed_out),
+            "peer_wait_timed_out": timed_out,
+            "against": "the same 36-layer int4 model (same seeds, same quantisation) on one GPU, one eager step "
+                       "from the same x at the same position"}
+
+
+def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float, parity: bool = True):
     """The 36-layer decoder chain (hidden 4096, 32 query / 8 KV heads of 128,
     intermediate 12288, int4 weights ~N(0,0.02), random-init) for one token at
     position 8191 (attention over a full 8192-token fp16 cache), sharded over
@@ -382,9 +556,13 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
     t0 = time.perf_counter()
     dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7)
     pos = cfg.ctx - 1
-    dec.buf.x.normal_()
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
+    check = decode_parity(dec, cfg, rank, world, device, pos) if (parity and world > 1) else None
+    if world > 1:
+        dist.barrier()
+    dec.buf.x.normal_()
+    torch.cuda.synchronize()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -425,6 +603,7 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
             "parallelism": (f"head/K-split shards x{world}, all-reduce x2 per layer ({exchange}: "
                             + ("NVLink peer stores" if exchange == "p2p" else "NCCL") + ")") if world > 1 else "1 GPU",
             "build_s": round(build_s, 1),
+            "parity": check,
             "model": "36 x (RmsNorm-GEMV-Rope QKV 6144x4096 + KV append, Att-full GQA 32/8 x 128, "
                      "O 4096x4096 + residual, RmsNorm-swiglu 2x12288x4096, down 4096x12288 + residual), int4"}
 
@@ -574,8 +753,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true", help="launch steps eagerly instead of from a CUDA graph")
     ap.add_argument("--no-pdl", action="store_true", help="plain launches (no programmatic dependent launch)")
+    ap.add_argument("--gemv-plan", default="auto", choices=["auto", "cluster", "per-sm", "per-sm-half"],
+                    help="single-vector GEMV kernel: chosen per shape, cluster split-K, or one CTA per SM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 36-layer decode-step measurement")
+    ap.add_argument("--no-decode-parity", action="store_true",
+                    help="skip the N>1 decode-step check against the same model on one GPU")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config measurements beside the headline (N=1)")
     ap.add_argument("--decode-steps", type=int, default=20)
     ap.add_argument("--clock-window", type=float, default=1.5, help="seconds of sampled load before timing")
     args = ap.parse_args()
@@ -601,11 +786,15 @@ def main():
     from vk_compute_b200 import ops
 
     ops.set_pdl(not args.no_pdl)
-    wl = build_workload(args.workload, rank, device)
+    ops.set_gemv_plan(args.gemv_plan)
+    wl = build_workload(args.workload, rank, device, world)
     step = wl["step"]
+    scaling = wl.get("scaling", "weak")
+    job_bytes = wl.get("job_bytes", world * wl["bytes"])
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
+    gw = gt = None
     if args.no_graph:
         warm = lambda: [step(i) for i in range(args.warmup)]
         timed = lambda: [step(args.warmup + i) for i in range(args.steps)]
@@ -613,10 +802,19 @@ def main():
         gw = capture(step, args.warmup, 0)
         gt = capture(step, args.steps, args.warmup)
         warm, timed = gw.replay, gt.replay
-    # sustained load with clock sampling, then the warm-up steps
+    # sustained load with clock sampling, then the warm-up steps.  Every rank
+    # makes the same number of replays (the sharded step holds a collective),
+    # so the count comes from one timed round agreed over the ranks first.
     sampler.start()
-    t_end = time.perf_counter() + args.clock_window
-    while time.perf_counter() < t_end:
+    t0 = time.perf_counter()
+    for _ in range(20):
+        warm()
+    torch.cuda.synchronize()
+    t_round = torch.tensor([time.perf_counter() - t0], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_round, op=dist.ReduceOp.MAX)
+    rounds = max(0, math.ceil(args.clock_window / max(float(t_round.item()), 1e-6)) - 1)
+    for _ in range(rounds):
         for _ in range(20):
             warm()
         torch.cuda.synchronize()
@@ -641,28 +839,31 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     per_step_s = ms_max / 1e3 / args.steps
-    value = world * wl["bytes"] / per_step_s / 1e9
+    value = job_bytes / per_step_s / 1e9
+    del gw, gt  # graphs holding collective launches go before the process group
 
-    # dominant kernel alone, back to back on the same stream
+    # dominant kernel alone, back to back on the same stream (no collective)
     dom = wl["dominant"]
     if wl["launches"] == 1:
         dom_s = per_step_s
-    else:
-        gd = capture(dom, args.steps, args.warmup) if not args.no_graph else None
+    elif args.no_graph:
         torch.cuda.synchronize()
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         d0.record(stream)
-        gd.replay() if gd is not None else [dom(args.warmup + i) for i in range(args.steps)]
+        for i in range(args.steps):
+            dom(args.warmup + i)
         d1.record(stream)
         torch.cuda.synchronize()
         dom_s = d0.elapsed_time(d1) / 1e3 / args.steps
+    else:
+        dom_s = time_launches(dom, args.steps, args.warmup)
     peak, peak_kind = peaks()
     achieved = wl["dominant_bytes"] / dom_s / 1e9
-    traffic = ncu_traffic(args.workload)
+    traffic = ncu_traffic(args.workload) if world == 1 else None
 
     e2e = None
     if wl["e2e"] is not None and args.workload in ("rmsnorm_gemv_int8", "gemv_fp16") and E2E_BIN.exists():
-        # the C host of the drop-in ABI (csrc/e2e_bench.c), one per rank
+        # the C host of the drop-in ABI (csrc/e2e_bench.c)
         K, N = wl["meta"]["K"], wl["meta"]["N"]
         opname = "RmsNorm-GEMV-INT8" if args.workload == "rmsnorm_gemv_int8" else "GEMV-FP16"
         env = dict(os.environ, VKC_DEVICE=str(local))
@@ -682,6 +883,16 @@ def main():
                "path": "C host (vkc_e2e_bench): writeBuffer + execute + readBuffer per step, reference ABI, "
                        "host wall clock, weight pool > 4x L2; execute timing events off (vkc_set_timing(0): "
                        "the program never calls getExecutionTime)"}
+    elif wl.get("e2e_sharded") is not None:
+        dt, hb, db = e2e_sharded(args, wl)
+        tt = torch.tensor([dt], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+        e2e = {"value": round(job_bytes / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": hb,
+               "d2h_bytes_per_step": db, "us_per_step": round(dt * 1e6, 2),
+               "path": "Python API (vk_compute_b200.ops + p2p) per rank: x host->device from pinned memory, "
+                       "the rank's RmsNorm-GEMV shard, NVLink all-gather of y, whole y device->host; host wall "
+                       "clock, max over ranks"}
     elif wl["e2e"] is not None:
         dt, hb, db = e2e_dropin(args, wl["e2e"], local)
         if world > 1:
@@ -691,42 +902,62 @@ def main():
         e2e = {"value": round(world * wl["bytes"] / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": hb,
                "d2h_bytes_per_step": db, "us_per_step": round(dt * 1e6, 2),
                "path": "Python ctypes: writeBuffer + execute + readBuffer per step, reference ABI, host wall clock"}
+    if "close" in wl:
+        wl["close"]()
+    dom_name, meta, launches = wl["dominant_name"], wl["meta"], wl["launches"]
+    bytes_rank, dom_bytes = wl["bytes"], wl["dominant_bytes"]
+    del wl, step, dom
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
 
     decode = None
     if not args.no_decode:
         torch.cuda.synchronize()
-        decode = decode_step_bench(rank, world, device, max(1, args.decode_steps), 3, peak)
+        decode = decode_step_bench(rank, world, device, max(1, args.decode_steps), 3, peak,
+                                   parity=not args.no_decode_parity)
 
-    cpu = None
+    configs = None
+    if world == 1 and args.workload == "rmsnorm_gemv_int8" and not args.no_configs:
+        configs = measure_configs(rank, device, args.steps, peak, local)
+
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_baseline(args.workload)
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        r = cpu_baseline(args.workload, budget_s=6.0, threads=1)
+        cpu1 = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if world > 1:
         dist.barrier()
     if rank == 0:
+        parallelism = "1 GPU"
+        if world > 1:
+            parallelism = (f"row shards x{world} of one matrix + NVLink all-gather of y" if scaling == "strong"
+                           else f"row shards x{world}, no collective")
         line = {
             "metric": f"{WORKLOADS[args.workload]} achieved HBM GB/s",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(per_step_s * 1e3, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "description": WORKLOADS[args.workload],
-                       "bytes_per_step": wl["bytes"], "per_rank": wl["meta"],
+                       "bytes_per_step": job_bytes, "bytes_per_rank_step": bytes_rank, "per_rank": meta,
                        "l2": "rotating weight pool >= 4x L2; each step reads weights last touched a full pool ago",
-                       "graph": not args.no_graph, "pdl": not args.no_pdl,
-                       "parallelism": f"row shards x{world}, no collective" if world > 1 else "1 GPU"},
+                       "graph": not args.no_graph, "pdl": not args.no_pdl, "gemv_plan": args.gemv_plan,
+                       "parallelism": parallelism},
             "frac_of_peak": round(value / world / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": wl["dominant_name"], "achieved": round(achieved, 2),
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 2),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "algorithmic_bytes": wl["dominant_bytes"],
+                         "traffic": traffic, "algorithmic_bytes": dom_bytes,
                          "us_per_launch": round(dom_s * 1e6, 3)},
-            "tensor": ({"achieved_tflops": round(wl["meta"]["flop"] / dom_s / 1e12, 2),
-                        "peak_tflops": tensor_peak(), "frac": round(wl["meta"]["flop"] / dom_s / 1e12 / tensor_peak(), 4)}
-                       if "flop" in wl["meta"] else None),
-            "gpu_launches": args.steps * wl["launches"],
+            "tensor": ({"achieved_tflops": round(meta["flop"] / dom_s / 1e12, 2),
+                        "peak_tflops": tensor_peak(), "frac": round(meta["flop"] / dom_s / 1e12 / tensor_peak(), 4)}
+                       if "flop" in meta else None),
+            "gpu_launches": args.steps * launches,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "cpu_baseline_single_thread": cpu1,
             "clocks": clocks,
+            "configs": configs,
             "decode_step": decode,
         }
         print(json.dumps(line), flush=True)

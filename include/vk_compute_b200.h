@@ -52,6 +52,17 @@ int vkc_get_pdl(void);
  * off, after which getExecutionTime returns 0. */
 void vkc_set_timing(int enable);
 int vkc_get_timing(void);
+/* Which kernel runs the single-vector GEMV family (vkc_gemv,
+ * vkc_rmsnorm_gemv, -rope, -rope_kv, -swiglu, vkc_gemv_residual / _peer):
+ * 0 (default) chooses per shape -- one 1024-thread CTA per SM, each with a
+ * balanced range of whole-K output columns, when every SM gets at least 16
+ * outputs and the input is not a peer exchange; otherwise clusters that split
+ * K and reduce in distributed shared memory.  1 always uses the cluster
+ * kernel; 2 uses the one-CTA-per-SM kernel with 1024-thread CTAs wherever it
+ * can run, 3 with 512-thread CTAs that leave half of each SM to the next
+ * launch.  Results agree to rounding.  No counterpart in the reference. */
+int vkc_set_gemv_plan(int plan);
+int vkc_get_gemv_plan(void);
 /* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
 int vkc_has_operator(const char* shader);
 /* Waits for the current device and returns its status word, whose flags
@@ -88,16 +99,20 @@ int vkc_gemv_residual(int bits, const void* w, const float* scale, const float* 
                       const float* residual, float* y, int N, int K, void* stream);
 
 /* RmsNorm-GEMV-Rope for a decoder's fused QKV projection with the KV-cache
- * append the reference lacks: outputs are [Q heads | K heads | V heads]
- * (q_rows, kv_rows, kv_rows rows, whole heads of head_dim); Q and K rotate on
- * adjacent pairs by pos*theta[p], V does not; all rows are written to y (fp32)
- * and K/V rows also, as fp16, at token `pos` into kcache K[t][h][d] and
- * vcache V[h][d/8][t][d%8] (the Att-full-FP16 layouts) of ctx_cap tokens. */
+ * append the reference lacks: outputs are q_rows of Q heads followed by
+ * kv_rows of K and kv_rows of V heads (whole heads of head_dim), laid out as
+ * [K heads | V heads] (kv_layout 0) or [K0 V0 | K1 V1 | ...] (kv_layout 1:
+ * with head_dim 128 each K/V pair is one 256-output scale block, so a shard
+ * holding whole pairs quantises exactly as the unsharded matrix does).  Q and
+ * K rotate on adjacent pairs by pos*theta[p], V does not; all rows are
+ * written to y (fp32) and K/V rows also, as fp16, at token `pos` into kcache
+ * K[t][h][d] and vcache V[h][d/8][t][d%8] (the Att-full-FP16 layouts) of
+ * ctx_cap tokens. */
 int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero,
                              const float* x, const float* gamma, const float* theta, float* y,
                              int N, int K, float eps, int rms_dim, int pos, int head_dim,
-                             int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
-                             void* stream);
+                             int q_rows, int kv_rows, int kv_layout, void* kcache, void* vcache,
+                             int ctx_cap, void* stream);
 
 /* RmsNorm-GEMV followed by a rotary epilogue at position `pos`.
  * rope_mode 0: the epilogue of shader/RmsNorm-GEMV-Rope-FP16.comp:76-89 as
@@ -158,8 +173,8 @@ int vkc_gemv_peer(int bits, const void* w, const float* scale, const float* zero
 int vkc_rmsnorm_gemv_rope_kv_peer(int bits, const void* w, const float* scale, const float* zero,
                                   const float* x_base, const vkc_peer_input* in, const float* gamma,
                                   const float* theta, float* y, int N, int K, float eps, int rms_dim,
-                                  int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
-                                  void* vcache, int ctx_cap, void* stream);
+                                  int pos, int head_dim, int q_rows, int kv_rows, int kv_layout,
+                                  void* kcache, void* vcache, int ctx_cap, void* stream);
 int vkc_rmsnorm_swiglu_peer(int bits, const void* wg, const float* sg, const float* zg, const void* wu,
                             const float* su, const float* zu, const float* x_base,
                             const vkc_peer_input* in, const float* gamma, float* h, int N, int K,
@@ -225,6 +240,20 @@ size_t vkc_attention_noalloc_max_scratch(void);
 int vkc_attention_decode_noalloc(const void* q, int q_bits, const void* kcache, const void* vcache,
                                  float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                                  void* stream);
+
+/* In-place RMSNorm of `rows` rows of `width` fp32 values each:
+ * x = x * inv_rms * gamma, inv_rms = 1/sqrt(sum(x^2)/width + eps), gamma has
+ * `width` values.  Replaces shader/RmsNorm.comp (width 256, eps 1e-5, one
+ * workgroup per row). */
+int vkc_rmsnorm_rows(float* x, const float* gamma, int rows, int width, float eps, void* stream);
+
+/* y[j] = sum_k x[k] W[k*N + j] for a plain row-major K x N fp32 matrix.
+ * Replaces shader/gemv2.comp and gemv3.comp, and gemv1.comp with N = K (the
+ * fp32 experiments that read W row-major rather than in 16-byte chunks;
+ * gemv4-gemv7 read the chunk layout and are served by vkc_gemv with bits 32).
+ * May use the library's per-device workspace (calls on different streams
+ * must then not overlap). */
+int vkc_gemv_rowmajor(const float* w, const float* x, float* y, int N, int K, void* stream);
 
 /* C = A B, row-major fp32 (A M x K, B K x N).  Replaces shader/gemm.comp. */
 int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, void* stream);

@@ -297,6 +297,20 @@ float vko_inv_rms(const float* x, int K, int rms_dim, float eps) {
     return (float)(1.0 / sqrt(ss / (double)rms_dim + (double)eps));
 }
 
+/* shader/RmsNorm.comp:22-52: in place, each row of `width` values (the
+ * shader's TS = 256, one workgroup per row) becomes (x * inv_rms) * gamma with
+ * inv_rms = 1/sqrt(sum(x^2)/width + eps) (EPSILON 1e-5, comp:9).  No CPU check
+ * exists in the reference; the formula is the shader's. */
+void vko_rmsnorm_rows(float* x, const float* gamma, int rows, int width, float eps) {
+    for (int r = 0; r < rows; ++r) {
+        float* xr = x + (int64_t)r * width;
+        double ss = 0.0;
+        for (int i = 0; i < width; ++i) ss += (double)xr[i] * xr[i];
+        const double inv = 1.0 / sqrt(ss / (double)width + (double)eps);
+        for (int i = 0; i < width; ++i) xr[i] = (float)((double)xr[i] * inv * gamma[i]);
+    }
+}
+
 /* shader/RmsNorm-GEMV-FP16.comp:36-73; CPU form src/compute.c:221-226. */
 void vko_rmsnorm_gemv(const float* x, const float* gamma, const float* w, int K, int N,
                       int rms_dim, float eps, float* y) {

@@ -50,6 +50,7 @@ void vko_fp16_matrix_to_float(const uint16_t* h, int64_t count, float* out);
 /* ---- operators (dense K x N weights, W[k*N + j]) ---- */
 void vko_gemv(const float* x, const float* w, int K, int N, float* y);
 float vko_inv_rms(const float* x, int K, int rms_dim, float eps);
+void vko_rmsnorm_rows(float* x, const float* gamma, int rows, int width, float eps);
 void vko_rmsnorm_gemv(const float* x, const float* gamma, const float* w, int K, int N,
                       int rms_dim, float eps, float* y);
 void vko_rope_reference(float* y, int N, int pos, const float* theta);

@@ -45,6 +45,7 @@ def lib() -> C.CDLL:
             "vko_fp16_matrix_to_float": (None, [_P, C.c_int64, _P]),
             "vko_gemv": (None, [_P, _P, i, i, _P]),
             "vko_inv_rms": (f, [_P, i, i, f]),
+            "vko_rmsnorm_rows": (None, [_P, _P, i, i, f]),
             "vko_rmsnorm_gemv": (None, [_P, _P, _P, i, i, i, f, _P]),
             "vko_rope_reference": (None, [_P, i, i, _P]),
             "vko_rope_pairs": (None, [_P, i, i, i, i, _P]),
@@ -151,6 +152,23 @@ def qswiglu(x, gamma, gate, up, bits: int, K: int, N: int, rms_dim: int | None =
                       _ptr(np.ascontiguousarray(dg)), _ptr(sg), _ptr(zg), _ptr(np.ascontiguousarray(du)),
                       _ptr(su), _ptr(zu), bits, K, N, rms_dim or K, eps, _ptr(h))
     return h
+
+
+def rmsnorm_rows(x: np.ndarray, gamma: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """shader/RmsNorm.comp on a copy of x ([rows][width])."""
+    y = np.array(x, np.float32)
+    rows, width = y.shape
+    lib().vko_rmsnorm_rows(_ptr(y), _ptr(np.ascontiguousarray(gamma, np.float32)), rows, width, eps)
+    return y
+
+
+def gemv_dense(x, w) -> np.ndarray:
+    """y = W^T x for a dense row-major K x N fp32 matrix (shader/gemv2.comp)."""
+    w = np.ascontiguousarray(w, np.float32)
+    K, N = w.shape
+    y = np.empty(N, np.float32)
+    lib().vko_gemv(_ptr(np.ascontiguousarray(x, np.float32)), _ptr(w), K, N, _ptr(y))
+    return y
 
 
 def inv_rms(x, rms_dim: int, eps: float) -> float:

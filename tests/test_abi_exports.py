@@ -41,7 +41,8 @@ REFERENCE_SHADERS = [
     "RmsNorm-GEMV-FP16.spv", "RmsNorm-GEMV-INT8.spv", "RmsNorm-GEMV-INT4.spv",
     "RmsNorm-GEMV-Rope-FP16.spv", "RmsNorm-GEMV-Rope-INT8.spv", "RmsNorm-GEMV-Rope-INT4.spv",
     "RmsNorm-swiglu-ffn.spv", "RmsNorm-swiglu-ffn-FP16.spv", "RmsNorm-swiglu-ffn-INT8.spv",
-    "RmsNorm-swiglu-ffn-INT4.spv", "Att-full-FP16.spv", "gemm.spv", "bin/GEMV-INT4.spv",
+    "RmsNorm-swiglu-ffn-INT4.spv", "Att-full-FP16.spv", "gemm.spv", "bin/GEMV-INT4.spv", "RmsNorm.spv",
+    "gemv1.spv", "gemv2.spv", "gemv3.spv", "gemv4.spv", "gemv5.spv", "gemv6.spv", "gemv7.spv",
     "shader\\gemm.comp",
 ]
 

@@ -20,6 +20,12 @@ def f16(a):
     return np.asarray(a, np.float32).astype(np.float16).astype(np.float64)
 
 
+def split_kv(qkv, q_rows, n_kv, hd):
+    """The model's QKV rows [Q | K0 V0 | K1 V1 | ...] reordered as [Q | K | V]."""
+    kv = qkv[q_rows:].reshape(n_kv, 2, hd)
+    return np.concatenate([qkv[:q_rows], kv[:, 0].ravel(), kv[:, 1].ravel()])
+
+
 def ref_attention(q, kc, vc, n_q, n_kv, hd, ctx, scale):
     """q [n_q*hd]; kc [cap][n_kv][hd]; vc [n_kv][hd/8][cap][8] (float)."""
     out = np.zeros(n_q * hd)
@@ -57,6 +63,7 @@ def test_decoder_two_layers_two_tokens():
         for i in range(cfg.layers):
             hl = host[i]
             qkv = o.qgemv(x, hl["g_attn"], *hl["q"][0], 4, H, cfg.qkv_rows, H, cfg.eps)
+            qkv = split_kv(qkv, q_rows, cfg.n_kv, hd)
             qkv = o.rope_pairs(qkv, hd, q_rows + kv_rows, pos, theta).astype(np.float64)
             hl["kc"][pos] = f16(qkv[q_rows:q_rows + kv_rows]).reshape(cfg.n_kv, hd)
             v = f16(qkv[q_rows + kv_rows:]).reshape(cfg.n_kv, hd // 8, 8)

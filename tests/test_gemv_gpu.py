@@ -17,6 +17,17 @@ from vk_compute_b200 import ops
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True, params=["cluster", "per-sm", "per-sm-half"])
+def gemv_plan(request):
+    """Every case runs on each single-vector kernel: clusters splitting K, and
+    one CTA per SM with whole-K column ranges in its full-SM (1024 threads)
+    and half-SM (512 threads) shapes, wherever those can run; the automatic
+    choice picks one of them per shape."""
+    ops.set_gemv_plan(request.param)
+    yield request.param
+    ops.set_gemv_plan("auto")
+
 BITS = [32, 16, 8, 4]
 
 # (K, N) per width: small, ragged/odd, and full-size shapes.
@@ -161,3 +172,56 @@ def test_invalid_arguments_are_rejected():
     bad = ops.PackedWeight(8, 1024, 500, w.packed, w.scale, w.zero)  # N not a multiple of 256
     with pytest.raises(VkcError):
         ops.gemv(bad, torch.zeros(1024, device="cuda"))
+
+
+def kv_split_order(q_rows, n_kv, hd, layout):
+    """Row indices that list a fused QKV output as [Q | K heads | V heads]."""
+    if layout == "split":
+        return np.arange(q_rows + 2 * n_kv * hd)
+    k = [q_rows + 2 * hd * h + d for h in range(n_kv) for d in range(hd)]
+    v = [q_rows + 2 * hd * h + hd + d for h in range(n_kv) for d in range(hd)]
+    return np.concatenate([np.arange(q_rows), k, v])
+
+
+@pytest.mark.parametrize("layout", ["split", "interleaved"])
+@pytest.mark.parametrize("bits,K,n_q,n_kv", [(4, 4096, 32, 8), (8, 1024, 8, 2), (16, 1024, 8, 2)])
+def test_qkv_rope_kv_append(layout, bits, K, n_q, n_kv):
+    """Fused QKV + RoPE + KV append: y against the oracle (Q and K rotated, V
+    not), and the caches hold exactly y's K and V rows as fp16 at `pos` (and
+    nothing anywhere else)."""
+    import torch
+    hd, cap, pos = 128, 64, 37
+    q_rows, kv_rows = n_q * hd, n_kv * hd
+    N = q_rows + 2 * kv_rows
+    theta = rope_theta(hd // 2, 1e6, hd)
+    x, g = device_vector(SEED_X, K), device_vector(SEED_GAMMA, K)
+    w = device_weight(SEED_W, K, N, bits)
+    kc = torch.zeros(cap, n_kv, hd, dtype=torch.float16, device="cuda")
+    vc = torch.zeros(n_kv, hd // 8, cap, 8, dtype=torch.float16, device="cuda")
+    y = ops.qkv_rope_append(w, x, g, torch.from_numpy(theta).cuda(), pos, head_dim=hd, q_rows=q_rows,
+                            kv_rows=kv_rows, kcache=kc, vcache=vc, ctx_cap=cap, kv_layout=layout)
+    d, s, z = host_weight(SEED_W, K, N, bits)
+    plain = o.qgemv(host_vector(SEED_X, K), host_vector(SEED_GAMMA, K), d, s, z, bits, K, N, K, 1e-6)
+    order = kv_split_order(q_rows, n_kv, hd, layout)
+    ref = o.rope_pairs(plain[order], hd, q_rows + kv_rows, pos, theta)
+    ys = y.cpu().numpy()[order]
+    assert_close(ys, ref, TOL[bits], f"QKV append bits={bits} layout={layout}")
+    y16 = torch.from_numpy(ys).half()
+    assert torch.equal(kc[pos].cpu(), y16[q_rows:q_rows + kv_rows].view(n_kv, hd))
+    assert torch.equal(vc[:, :, pos].cpu(), y16[q_rows + kv_rows:].view(n_kv, hd // 8, 8))
+    kc[pos] = 0
+    vc[:, :, pos] = 0
+    assert not kc.any() and not vc.any(), "the append wrote outside token pos"
+
+
+@pytest.mark.parametrize("bits,K,N", [(4, 12288, 4096), (8, 1024, 512), (16, 4096, 4096)])
+def test_gemv_residual(bits, K, N):
+    import torch
+    x = device_vector(SEED_X, K)
+    res = device_vector(SEED_GAMMA, N)
+    w = device_weight(SEED_W, K, N, bits)
+    y = ops.gemv_residual(w, x, res).cpu().numpy()
+    d, s, z = host_weight(SEED_W, K, N, bits)
+    ref = o.qgemv(host_vector(SEED_X, K), None, d, s, z, bits, K, N) + host_vector(SEED_GAMMA, N)
+    assert_close(y, ref, TOL[bits], f"GEMV + residual bits={bits} K={K} N={N}")
+    assert torch.isfinite(torch.from_numpy(y)).all()

@@ -2,10 +2,11 @@
 against the expected concatenation and the peer all-reduce with residual
 against the rank-ordered sum, both eager and replayed from a CUDA graph, and
 the sharded decoder chain at world 2 (peer and NCCL all-reduces) against the
-same model on one GPU.  The chain test uses fp16 weights: with int4/int8
-weights the head-permuted QKV shard is quantised in other 256-row scale
-blocks than the unsharded matrix, so the models differ by quantisation
-rounding (the K-split O and down projections keep their scales exactly)."""
+same model on one GPU, with fp16 and with int4 weights.  Every shard is made
+of whole 256-row scale blocks of the unsharded matrices (the QKV rows are
+[Q | K0 V0 | K1 V1 | ...]), so the int4 model is quantised identically on one
+and on two GPUs and the outputs differ only by the order of the cross-rank
+sums."""
 import os
 import socket
 import tempfile
@@ -128,12 +129,15 @@ def _gather_child(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def _decode_child(rank, world, port, out_dir, exchange):
+DECODE_CFG = dict(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64)
+
+
+def _decode_child(rank, world, port, out_dir, exchange, bits):
     dist = _init(rank, world, port)
     from vk_compute_b200.decode import DecoderConfig, ShardedDecoder
 
     dev = torch.device("cuda", rank)
-    cfg = DecoderConfig(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64, bits=16)
+    cfg = DecoderConfig(**DECODE_CFG, bits=bits)
     dec = ShardedDecoder(cfg, rank=rank, world=world, device=dev, seed=5, exchange=exchange)
     x0 = torch.Generator().manual_seed(9)
     dec.buf.x.copy_(torch.randn(cfg.hidden, generator=x0).to(dev))
@@ -185,16 +189,17 @@ def test_p2p_allgather_two_gpus():
 
 
 @needs2
+@pytest.mark.parametrize("bits", [16, 4])
 @pytest.mark.parametrize("exchange", ["p2p", "p2p-kernel", "nccl"])
-def test_sharded_decoder_matches_one_gpu(exchange):
+def test_sharded_decoder_matches_one_gpu(exchange, bits):
     from vk_compute_b200.decode import DecoderConfig, ShardedDecoder
 
     with tempfile.TemporaryDirectory() as d:
-        _run(_decode_child, 2, d, exchange)
+        _run(_decode_child, 2, d, exchange, bits)
         got = np.load(os.path.join(d, f"dec_{exchange}.npy"))
         for r in range(2):
             assert open(os.path.join(d, f"dec_{exchange}_{r}.status")).read() == "ok"
-    cfg = DecoderConfig(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64, bits=16)
+    cfg = DecoderConfig(**DECODE_CFG, bits=bits)
     dec = ShardedDecoder(cfg, seed=5, device="cuda:0")
     x0 = torch.Generator().manual_seed(9)
     dec.buf.x.copy_(torch.randn(cfg.hidden, generator=x0).cuda())
@@ -202,4 +207,5 @@ def test_sharded_decoder_matches_one_gpu(exchange):
         ref = dec.step(pos)
     ref = ref.cpu().numpy()
     err = np.abs(got - ref).max() / np.abs(ref).max()
-    assert err < 1e-5, f"sharded ({exchange}) vs one GPU: {err}"
+    # the same model on both sides: only the cross-rank sum order differs
+    assert err < (1e-5 if bits == 16 else 1e-4), f"sharded ({exchange}, {bits}-bit) vs one GPU: {err}"

@@ -25,17 +25,22 @@ SIGNATURES = {
     "vkc_has_operator": (_i, [C.c_char_p]),
     "vkc_device_status": (_i, [C.POINTER(C.c_uint), _i]),
     "vkc_wait_limits": (None, [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "vkc_set_gemv_plan": (_i, [_i]),
+    "vkc_get_gemv_plan": (_i, []),
     "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),
     "vkc_rmsnorm_gemv": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
     "vkc_rmsnorm_gemv_rope": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p]),
     "vkc_rmsnorm_swiglu": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
     "vkc_gemv_residual": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _p]),
-    "vkc_rmsnorm_gemv_rope_kv": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p, _p, _i, _p]),
+    "vkc_rmsnorm_gemv_rope_kv": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _i, _p, _p, _i,
+                                      _p]),
     "vkc_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "vkc_attention_decode": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_attention_decode_cache": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_attention_decode_append": (_i, [_p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "vkc_gemm_f32": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "vkc_rmsnorm_rows": (_i, [_p, _p, _i, _i, _f, _p]),
+    "vkc_gemv_rowmajor": (_i, [_p, _p, _p, _i, _i, _p]),
     "vkc_gemm_bf16": (_i, [_p, _p, _p, _i, _i, _i, _p]),
     "vkc_gemm_bf16_status": (_i, [C.POINTER(C.c_uint), _i]),
     "vkc_generate": (_i, [_i, _i, _i, _i, _p, _p]),
@@ -50,8 +55,8 @@ SIGNATURES = {
     "vkc_gemv_peer": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
     "vkc_gemv_batched": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _i, _p]),
     "vkc_rmsnorm_gemv_batched": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _f, _i, _p]),
-    "vkc_rmsnorm_gemv_rope_kv_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _p,
-                                           _p, _i, _p]),
+    "vkc_rmsnorm_gemv_rope_kv_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _i, _i, _i, _i, _i,
+                                           _p, _p, _i, _p]),
     "vkc_rmsnorm_swiglu_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
 }
 

@@ -1304,7 +1304,7 @@ int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const vo
         const size_t need = attention_workspace_bytes(n_q > 0 ? n_q : 1, n_kv > 0 ? n_kv : 1,
                                                       head_dim > 0 ? head_dim : 8, ctx > 0 ? ctx : 1);
         void* base = nullptr;
-        if (int e = device_workspace(need + kWorkspaceHeader, &base, s)) return e;
+        if (int e = device_workspace(need + kWorkspaceHeader, &base, s, kWorkspaceAttention)) return e;
         workspace = static_cast<char*>(base) + kWorkspaceHeader;
         workspace_bytes = need;
     }
@@ -1320,7 +1320,7 @@ int vkc_attention_decode_cache(const void* q, int q_bits, const void* kcache, co
         const size_t need = attention_workspace_bytes(n_q > 0 ? n_q : 1, n_kv > 0 ? n_kv : 1,
                                                       head_dim > 0 ? head_dim : 8, ctx > 0 ? ctx : 1);
         void* base = nullptr;
-        if (int e = device_workspace(need + kWorkspaceHeader, &base, s)) return e;
+        if (int e = device_workspace(need + kWorkspaceHeader, &base, s, kWorkspaceAttention)) return e;
         workspace = static_cast<char*>(base) + kWorkspaceHeader;
         workspace_bytes = need;
     }

@@ -82,13 +82,14 @@ struct GemvParams {
     int head_dim;
     int rot_rows;
     const float* residual;  // optional: y[j] += residual[j] (plain GEMV)
-    // Optional KV-cache append (rotary-pairs mode): outputs [q_rows, q_rows +
-    // kv_rows) are K heads, the next kv_rows are V heads; both are also stored
-    // as fp16 at token `pos` into K[t][h][d] and V[h][d/8][t][d%8] caches of
-    // `ctx_cap` tokens.
+    // Optional KV-cache append (rotary-pairs mode): the outputs after the
+    // first q_rows are K and V heads, [K heads | V heads] (kv_interleave 0) or
+    // [K0 V0 | K1 V1 | ...] (kv_interleave 1); both are also stored as fp16 at
+    // token `pos` into K[t][h][d] and V[h][d/8][t][d%8] caches of `ctx_cap`
+    // tokens.
     uint16_t* kcache;
     uint16_t* vcache;
-    int q_rows, kv_rows, ctx_cap;
+    int q_rows, kv_rows, ctx_cap, kv_interleave;
     // Peer output (plain GEMV, K-split shard): output j goes, as the 8-byte
     // word (flag << 32 | float bits), to element prank*N + j of every rank's
     // [pworld][N] word buffer (peer_slots: device array of pworld pointers),
@@ -215,7 +216,10 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
         }
     } else if constexpr (MODE == kRopePairs) {
         const float partner = __shfl_xor_sync(0xffffffffu, out, 1);
-        if (active && j < p.rot_rows) {
+        // Q and K rows rotate, V rows do not
+        const bool rot = p.kv_interleave ? (j < p.q_rows || (j - p.q_rows) % (2 * p.head_dim) < p.head_dim)
+                                         : j < p.rot_rows;
+        if (active && rot) {
             float sa, ca;
             sincosf(static_cast<float>(p.pos) * p.theta[(j % p.head_dim) >> 1], &sa, &ca);
             out = (j & 1) == 0 ? out * ca - partner * sa : partner * sa + out * ca;
@@ -237,17 +241,24 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
             p.y[j] = out;
         }
         if constexpr (MODE == kRopePairs) {
-            if (p.kcache && j >= p.q_rows) {
+            if (p.kcache && j >= p.q_rows && j < p.q_rows + 2 * p.kv_rows) {
                 const int jj = j - p.q_rows;
                 const int hd = p.head_dim;
                 const uint16_t bits = __half_as_ushort(__float2half_rn(out));
-                if (jj < p.kv_rows) {
-                    const int h = jj / hd, d = jj % hd;
-                    p.kcache[(static_cast<size_t>(p.pos) * (p.kv_rows / hd) + h) * hd + d] = bits;
-                } else if (jj < 2 * p.kv_rows) {
-                    const int h = (jj - p.kv_rows) / hd, d = (jj - p.kv_rows) % hd;
-                    p.vcache[((static_cast<size_t>(h) * (hd / 8) + d / 8) * p.ctx_cap + p.pos) * 8 + d % 8] = bits;
+                int h, d;
+                bool is_k;
+                if (p.kv_interleave) {
+                    const int w = jj % (2 * hd);
+                    h = jj / (2 * hd);
+                    is_k = w < hd;
+                    d = w % hd;
+                } else {
+                    is_k = jj < p.kv_rows;
+                    h = (is_k ? jj : jj - p.kv_rows) / hd;
+                    d = jj % hd;
                 }
+                if (is_k) p.kcache[(static_cast<size_t>(p.pos) * (p.kv_rows / hd) + h) * hd + d] = bits;
+                else p.vcache[((static_cast<size_t>(h) * (hd / 8) + d / 8) * p.ctx_cap + p.pos) * 8 + d % 8] = bits;
             }
         }
     }
@@ -492,6 +503,219 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
                 tot[1] += rp[NS * C + 1];
                 tot[2] += rp[NS * C + 2];
             }
+        }
+        finalize<MODE, NS, kQuant, kNorm>(p, col0 + tid, active, a, tot);
+    }
+}
+
+// ---- One CTA per SM: balanced column ranges, all of K per CTA ------------
+// For matrices wide enough to give every SM at least 16 outputs.  The grid is
+// exactly one CTA per SM, so every SM streams the same number of bytes: the
+// CTAs of a scale block
+// split its 256 outputs into even-aligned ranges, blocks getting
+// floor(or ceil)(SMs / blocks) CTAs, which balances the SMs to within a few
+// percent at the decode shapes.  Each CTA reads all of K for its columns, so
+// the RMS sum, the zero-point constant and the whole dot product stay inside
+// the CTA: no cluster, no split-K reduction, deterministic sums.  Streaming
+// and arithmetic are those of gemv_kernel (per-thread cp.async rings, folded
+// scales, exact code conversion); the C outputs times G row groups fill the
+// CTA's threads.
+//
+// Two shapes of CTA.  T = 1024 threads hold all of an SM's registers, so a
+// launch has the SMs to itself.  T = 512 threads with at most half an SM's
+// shared memory leave room for the next launch in the stream: under
+// programmatic dependent launch its CTA becomes resident beside this one,
+// primes its ring (its weights do not depend on this kernel) and waits, so
+// consecutive launches overlap their first bytes with the previous tail.
+constexpr int kSmThreadsMax = 1024;
+constexpr int kSmHalfSmem = 112 * 1024;  // shared memory that lets two CTAs share an SM
+
+// Column range [col0, col0 + C) of CTA `cta` of `ctas` (see above); fp32 and
+// fp16 weights have no scale blocks and split N evenly in pairs.
+__device__ __forceinline__ void sm_columns(int N, bool blocks, int cta, int ctas, int& col0, int& C) {
+    if (blocks) {
+        const int nb = N / kGroup;
+        const int base = ctas / nb, extra = ctas % nb;
+        int b, m, per;
+        if (cta < extra * (base + 1)) {
+            per = base + 1;
+            b = cta / per;
+            m = cta % per;
+        } else {
+            per = base;
+            const int i = cta - extra * (base + 1);
+            b = extra + i / per;
+            m = i % per;
+        }
+        const int lo = 2 * ((m * (kGroup / 2)) / per), hi = 2 * (((m + 1) * (kGroup / 2)) / per);
+        col0 = b * kGroup + lo;
+        C = hi - lo;
+    } else {
+        const int pairs = N / 2;
+        const int lo = static_cast<int>((static_cast<long long>(cta) * pairs) / ctas);
+        const int hi = static_cast<int>((static_cast<long long>(cta + 1) * pairs) / ctas);
+        col0 = 2 * lo;
+        C = 2 * (hi - lo);
+    }
+}
+
+template <int BITS, int MODE, int kSmThreads, int D>
+__global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_sm_kernel(const GemvParams p) {
+    constexpr int NS = MODE == kSwiglu ? 2 : 1;
+    constexpr int KPC = 128 / BITS;
+    constexpr bool kQuant = BITS <= 8;
+    constexpr bool kNorm = MODE != kGemv;
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* ring = reinterpret_cast<uint4*>(smem);                                  // [NS][D][1024]
+    float* xs = reinterpret_cast<float*>(smem + NS * D * kSmThreads * 16);         // [R][NS][KPC]
+    float* red = reinterpret_cast<float*>(smem);                                   // [NS][G][C], after the stream
+    __shared__ float wred[kSmThreads / 32][3];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int col0, C;
+    sm_columns(p.N, kQuant, blockIdx.x, gridDim.x, col0, C);
+    const int G = kSmThreads / C;
+    const int c = tid % C, grp = tid / C;
+    const bool streams = grp < G;  // the last threads (fewer than C) only stage activations
+    const int col = col0 + c;
+    const int nk = p.K;
+    const size_t sblk = static_cast<size_t>(col0 / kGroup) * p.K;
+
+    pdl_launch_dependents();
+
+    // ---- activations: gamma / scale / zero before the weight stream, x after
+    // the dependency wait; passes of 4096 values held in registers.
+    constexpr int kMaxAct = 4;
+    float av_g[kMaxAct], av_s[NS][kMaxAct], av_z[NS][kMaxAct], av_x[kMaxAct];
+    auto load_acts = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int k = base + tid + q * kSmThreads;
+            const bool ok = k < nk;
+            av_g[q] = (kNorm && ok) ? __ldg(p.gamma + k) : 1.f;
+#pragma unroll
+            for (int st = 0; st < NS; ++st) {
+                av_s[st][q] = (kQuant && ok) ? __ldg(p.s[st] + sblk + k) : 1.f;
+                av_z[st][q] = (kQuant && ok) ? __ldg(p.z[st] + sblk + k) : 0.f;
+            }
+        }
+    };
+    auto load_x = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int k = base + tid + q * kSmThreads;
+            av_x[q] = k < nk ? p.x[k] : 0.f;
+        }
+    };
+    float ss = 0.f, cz[NS];
+#pragma unroll
+    for (int st = 0; st < NS; ++st) cz[st] = 0.f;
+    auto fold = [&](int base) {
+#pragma unroll
+        for (int q = 0; q < kMaxAct; ++q) {
+            const int k = base + tid + q * kSmThreads;
+            if (k < nk) {
+                const float xv = av_x[q];
+                float xg = xv;
+                if constexpr (kNorm) {
+                    ss = fmaf(xv, xv, ss);
+                    xg = xv * av_g[q];
+                }
+                const int rl = k / KPC, i = k % KPC;
+#pragma unroll
+                for (int st = 0; st < NS; ++st) {
+                    float v = xg;
+                    if constexpr (kQuant) {
+                        v = xg * av_s[st][q];
+                        cz[st] = fmaf(xg, av_z[st][q], cz[st]);
+                    }
+                    if constexpr (BITS == 4) v *= int4_prescale(i);
+                    xs[(rl * NS + st) * KPC + i] = v;
+                }
+            }
+        }
+    };
+    load_acts(0);
+
+    // ---- weights: prime the ring with D rows per thread -------------------
+    const int my_rows = streams && grp < p.R ? (p.R - grp + G - 1) / G : 0;  // rows grp, grp+G, ...
+    auto src = [&](int st, int i) {
+        const int r = grp + i * G;
+        return reinterpret_cast<const uint4*>(p.w[st]) + (static_cast<size_t>(r) * p.N + col);
+    };
+    auto slot = [&](int st, int i) { return smem_addr(ring + (st * D + (i % D)) * kSmThreads + tid); };
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+        if (i < my_rows)
+#pragma unroll
+            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i), src(st, i));
+        cp_async_commit();
+    }
+
+    // ---- x depends on the previous kernel: wait for it, then fold --------
+    pdl_wait();
+    load_x(0);
+    fold(0);
+    for (int base = kMaxAct * kSmThreads; base < nk; base += kMaxAct * kSmThreads) {
+        load_acts(base);
+        load_x(base);
+        fold(base);
+    }
+    __syncthreads();
+
+    // ---- stream this thread's rows through its ring ------------------------
+    uint64_t acc[NS][4];
+#pragma unroll
+    for (int st = 0; st < NS; ++st) acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0ull;
+    for (int i = 0; i < my_rows; ++i) {
+        cp_async_wait<D - 1>();
+        const int rl = grp + i * G;
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+            const uint4 chunk = ring[(st * D + (i % D)) * kSmThreads + tid];
+            chunk_fma<BITS>(chunk, xs + (rl * NS + st) * KPC, acc[st]);
+        }
+        if (i + D < my_rows)
+#pragma unroll
+            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i + D), src(st, i + D));
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+
+    // ---- reduce the row groups of each column and the CTA's scalars --------
+    {
+        const float w0 = warp_sum(ss), w1 = warp_sum(cz[0]), w2 = NS == 2 ? warp_sum(cz[NS - 1]) : 0.f;
+        if (lane == 0) {
+            wred[warp][0] = w0;
+            wred[warp][1] = w1;
+            wred[warp][2] = w2;
+        }
+    }
+    __syncthreads();  // every thread's ring reads are done: the ring becomes `red`
+    if (streams) {
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+            const float2 a = f2_unpack(acc[st][0]), b = f2_unpack(acc[st][1]);
+            const float2 c2 = f2_unpack(acc[st][2]), d = f2_unpack(acc[st][3]);
+            red[(st * G + grp) * C + c] = ((a.x + a.y) + (b.x + b.y)) + ((c2.x + c2.y) + (d.x + d.y));
+        }
+    }
+    __syncthreads();
+    if (warp * 32 < C) {
+        const bool active = tid < C;
+        float a[NS], tot[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+            a[st] = 0.f;
+            if (active)
+                for (int g = 0; g < G; ++g) a[st] += red[(st * G + g) * C + tid];
+        }
+#pragma unroll
+        for (int w = 0; w < kSmThreads / 32; ++w) {
+            tot[0] += wred[w][0];
+            tot[1] += wred[w][1];
+            tot[2] += wred[w][2];
         }
         finalize<MODE, NS, kQuant, kNorm>(p, col0 + tid, active, a, tot);
     }
@@ -1034,6 +1258,91 @@ int sm_count(int* out) {
     return kOk;
 }
 
+// Which single-vector GEMV kernel runs (vkc_set_gemv_plan): 0 chooses per
+// shape, 1 always the cluster split-K kernel, 2 the one-CTA-per-SM kernel in
+// its full-SM shape wherever it can run, 3 the same in its half-SM shape.
+int g_gemv_plan = 0;
+
+constexpr size_t kSmMaxDynamicSmem = 220 * 1024;
+
+// Shared memory of a per-SM CTA: the ring (NS streams x D rows x T threads
+// x 16 bytes) and the staged activations (NS x K floats).
+inline size_t sm_smem_bytes(int NS, int T, int D, int K) {
+    return static_cast<size_t>(NS) * D * T * 16 + static_cast<size_t>(NS) * K * 4;
+}
+
+// Shape of a per-SM launch: threads and ring depth.  The half-SM shape (512
+// threads) takes the deepest ring that keeps two CTAs on an SM; when even the
+// shallowest does not fit beside the staged activations, the full-SM shape.
+struct SmShape {
+    int T = 0, D = 0;
+    size_t smem = 0;
+};
+
+SmShape sm_shape(int NS, int K, bool half) {
+    SmShape sh;
+    if (half) {
+        const int depths[] = {12, 8, 4};
+        for (int d : depths) {
+            if (NS == 2 && d > 4) continue;  // 64 KB ring for two streams
+            const size_t b = sm_smem_bytes(NS, 512, d, K);
+            if (b + 1024 <= static_cast<size_t>(kSmHalfSmem)) {
+                sh.T = 512;
+                sh.D = d;
+                sh.smem = b;
+                return sh;
+            }
+        }
+    }
+    sh.T = 1024;
+    sh.D = NS == 1 ? 8 : 4;
+    sh.smem = sm_smem_bytes(NS, 1024, sh.D, K);
+    return sh;
+}
+
+// The per-SM kernel serves a shape when every SM gets at least 16 outputs (at
+// least one CTA per scale block), the staged activations fit in shared memory
+// beside the ring, and the input is not a peer exchange (its per-element
+// waits would be repeated by every CTA).
+template <int BITS, int MODE>
+bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh) {
+    if (p.xslots || p.N % 2 != 0 || sh.smem > kSmMaxDynamicSmem) return false;
+    // every CTA gets at least one pair of outputs, and at most T - 2 outputs
+    if (BITS <= 8 && (p.N / kGroup > sms || (sms + p.N / kGroup - 1) / (p.N / kGroup) > kGroup / 2)) return false;
+    if (BITS > 8 && (p.N / 2 < sms || p.N / sms > sh.T - 2)) return false;
+    if (g_gemv_plan >= 2) return true;
+    return p.N >= 16 * sms;
+}
+
+template <int BITS, int MODE, int T, int D>
+int launch_sm_shape(const GemvParams& p, cudaStream_t stream, int sms, size_t smem) {
+    const void* kern = reinterpret_cast<const void*>(gemv_sm_kernel<BITS, MODE, T, D>);
+    if (int e = ensure_smem(kern, smem)) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms, 1, 1);
+    cfg.blockDim = dim3(T, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    cfg.attrs = attrs;
+    cfg.numAttrs = launch_attrs(attrs, 1);
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_sm_kernel<BITS, MODE, T, D>, p));
+    return kOk;
+}
+
+template <int BITS, int MODE>
+int launch_sm(const GemvParams& p0, cudaStream_t stream, int sms, const SmShape& sh) {
+    constexpr int NS = MODE == kSwiglu ? 2 : 1;
+    GemvParams p = p0;
+    p.R = p.K / (128 / BITS);
+    if (sh.T == 1024) return launch_sm_shape<BITS, MODE, 1024, NS == 1 ? 8 : 4>(p, stream, sms, sh.smem);
+    if constexpr (NS == 1) {
+        if (sh.D == 12) return launch_sm_shape<BITS, MODE, 512, 12>(p, stream, sms, sh.smem);
+        if (sh.D == 8) return launch_sm_shape<BITS, MODE, 512, 8>(p, stream, sms, sh.smem);
+    }
+    return launch_sm_shape<BITS, MODE, 512, 4>(p, stream, sms, sh.smem);
+}
+
 template <int BITS, int MODE>
 int launch_one(const GemvParams& p0, cudaStream_t stream) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
@@ -1042,6 +1351,10 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     p.R = p.K / KPC;
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
+    if (g_gemv_plan != 1) {
+        const SmShape sh = sm_shape(NS, p.K, g_gemv_plan != 2);
+        if (sm_kernel_fits<BITS, MODE>(p, sms, sh)) return launch_sm<BITS, MODE>(p, stream, sms, sh);
+    }
     // Widest tile and smallest cluster that put at least two CTAs on every SM.
     int C = 32, S = 8;
     bool found = false;
@@ -1376,8 +1689,8 @@ static int set_peer_input(GemvParams& p, const vkc_peer_input* in) {
 
 static int rope_kv_impl(int bits, const void* w, const float* scale, const float* zero, const float* x,
                         const float* gamma, const float* theta, float* y, int N, int K, float eps, int rms_dim,
-                        int pos, int head_dim, int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
-                        void* stream, const vkc_peer_input* in) {
+                        int pos, int head_dim, int q_rows, int kv_rows, int kv_layout, void* kcache, void* vcache,
+                        int ctx_cap, void* stream, const vkc_peer_input* in) {
     if (!gamma || !theta || !kcache || !vcache) return set_error(kErrArg, "null gamma, theta or cache");
     if (int e = check_common(bits, N, K, w, scale, zero, x, y, gamma)) return e;
     if (rms_dim <= 0) return set_error(kErrArg, "rms_dim=%d must be positive", rms_dim);
@@ -1387,6 +1700,7 @@ static int rope_kv_impl(int bits, const void* w, const float* scale, const float
         return set_error(kErrArg, "rows must be q_rows + 2*kv_rows = N in whole heads (q=%d kv=%d N=%d)", q_rows,
                          kv_rows, N);
     if (pos < 0 || pos >= ctx_cap) return set_error(kErrArg, "pos=%d outside the cache of %d tokens", pos, ctx_cap);
+    if (kv_layout != 0 && kv_layout != 1) return set_error(kErrArg, "kv_layout=%d (expected 0 or 1)", kv_layout);
     GemvParams p = {};
     p.w[0] = static_cast<const uint8_t*>(w);
     p.s[0] = scale;
@@ -1406,6 +1720,7 @@ static int rope_kv_impl(int bits, const void* w, const float* scale, const float
     p.vcache = static_cast<uint16_t*>(vcache);
     p.q_rows = q_rows;
     p.kv_rows = kv_rows;
+    p.kv_interleave = kv_layout;
     p.ctx_cap = ctx_cap;
     if (int e = set_peer_input(p, in)) return e;
     return launch_mode<kRopePairs>(bits, p, static_cast<cudaStream_t>(stream));
@@ -1413,20 +1728,20 @@ static int rope_kv_impl(int bits, const void* w, const float* scale, const float
 
 int vkc_rmsnorm_gemv_rope_kv(int bits, const void* w, const float* scale, const float* zero, const float* x,
                              const float* gamma, const float* theta, float* y, int N, int K, float eps,
-                             int rms_dim, int pos, int head_dim, int q_rows, int kv_rows, void* kcache,
-                             void* vcache, int ctx_cap, void* stream) {
+                             int rms_dim, int pos, int head_dim, int q_rows, int kv_rows, int kv_layout,
+                             void* kcache, void* vcache, int ctx_cap, void* stream) {
     return rope_kv_impl(bits, w, scale, zero, x, gamma, theta, y, N, K, eps, rms_dim, pos, head_dim, q_rows, kv_rows,
-                        kcache, vcache, ctx_cap, stream, nullptr);
+                        kv_layout, kcache, vcache, ctx_cap, stream, nullptr);
 }
 
 int vkc_rmsnorm_gemv_rope_kv_peer(int bits, const void* w, const float* scale, const float* zero,
                                   const float* x_base, const vkc_peer_input* in, const float* gamma,
                                   const float* theta, float* y, int N, int K, float eps, int rms_dim, int pos,
-                                  int head_dim, int q_rows, int kv_rows, void* kcache, void* vcache, int ctx_cap,
-                                  void* stream) {
+                                  int head_dim, int q_rows, int kv_rows, int kv_layout, void* kcache,
+                                  void* vcache, int ctx_cap, void* stream) {
     if (!in) return set_error(kErrArg, "null peer input");
     return rope_kv_impl(bits, w, scale, zero, x_base, gamma, theta, y, N, K, eps, rms_dim, pos, head_dim, q_rows,
-                        kv_rows, kcache, vcache, ctx_cap, stream, in);
+                        kv_rows, kv_layout, kcache, vcache, ctx_cap, stream, in);
 }
 
 int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* zero, const float* x,
@@ -1558,6 +1873,13 @@ int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const 
 
 // Status word of the current device (bits: kStatus*).  Reading waits for the
 // device; `clear` resets it.
+int vkc_set_gemv_plan(int plan) {
+    if (plan < 0 || plan > 3) return set_error(kErrArg, "GEMV plan %d (expected 0 to 3)", plan);
+    g_gemv_plan = plan;
+    return kOk;
+}
+int vkc_get_gemv_plan(void) { return g_gemv_plan; }
+
 void vkc_wait_limits(uint64_t* peer_ns, uint64_t* cluster_ns) {
     if (peer_ns) *peer_ns = kPeerWaitNs;
     if (cluster_ns) *cluster_ns = kClusterWaitNs;

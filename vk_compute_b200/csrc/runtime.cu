@@ -53,15 +53,16 @@ struct DeviceScratch {
     size_t bytes = 0;
 };
 std::mutex g_scratch_mu;
-DeviceScratch g_scratch[64];
+DeviceScratch g_scratch[64][kWorkspaceUsers];
 }  // namespace
 
-int device_workspace(size_t bytes, void** out, cudaStream_t stream) {
+int device_workspace(size_t bytes, void** out, cudaStream_t stream, int user) {
     int dev = 0;
     VKC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
+    if (user < 0 || user >= kWorkspaceUsers) return set_error(kErrArg, "workspace user %d", user);
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    DeviceScratch& w = g_scratch[dev];
+    DeviceScratch& w = g_scratch[dev][user];
     if (w.bytes < bytes) {
         // Grow to at least 4 MiB so the usual shapes allocate once.
         size_t want = bytes < (4u << 20) ? (4u << 20) : bytes;
@@ -196,7 +197,8 @@ Ctx* ctx_of(const void* handle) {
 // ---------------------------------------------------------------------------
 // Operator registry: reference shader name -> launcher
 // ---------------------------------------------------------------------------
-enum OpKind { kOpGemv, kOpRmsGemv, kOpRope, kOpSwiglu, kOpAttention, kOpGemm };
+enum OpKind { kOpGemv, kOpRmsGemv, kOpRope, kOpSwiglu, kOpAttention, kOpGemm, kOpRmsNorm, kOpGemvRowMajor,
+              kOpGemvSquare };
 
 struct OpInfo {
     const char* name;  // shader base name, without directory or extension
@@ -212,8 +214,23 @@ struct OpInfo {
 //   swiglu            {x, gamma, G, U, y [, sG, zG, sU, zU]}  shader/RmsNorm-swiglu-ffn-INT4.comp:20-28
 //   Att-full-FP16     {K, V, Q, y}                   shader/Att-full-FP16.comp:21-24
 //   gemm              {A, B, C}                      shader/gemm.comp:12-14
+//   RmsNorm           {x (in place), gamma}          shader/RmsNorm.comp:11-17
+//   gemv1..gemv7      {A (x), B (W), C (y)}          shader/gemv1.comp:12-14 ... gemv7.comp:15-17
+// gemv4-gemv7 read W in the 16-byte chunk layout of gemv.comp (vec4 B[row*N +
+// col], four consecutive k of one column: gemv4.comp:36-37, gemv5.comp:37-38,
+// gemv6.comp:36-40, gemv7.comp:49-52); gemv2 and gemv3 read a row-major K x N
+// W (B[row*N + col], gemv2.comp:35, gemv3.comp:37-38); gemv1 a square
+// row-major K x K W with K outputs (B[(t*TS + k)*K + col], gemv1.comp:29-35).
 const OpInfo kOps[] = {
     {"gemv", kOpGemv, 32},
+    {"gemv1", kOpGemvSquare, 32},
+    {"gemv2", kOpGemvRowMajor, 32},
+    {"gemv3", kOpGemvRowMajor, 32},
+    {"gemv4", kOpGemv, 32},
+    {"gemv5", kOpGemv, 32},
+    {"gemv6", kOpGemv, 32},
+    {"gemv7", kOpGemv, 32},
+    {"rmsnorm", kOpRmsNorm, 32},
     {"gemv-fp32", kOpGemv, 32},
     {"gemv-fp16", kOpGemv, 16},
     {"gemv-int8", kOpGemv, 8},
@@ -251,6 +268,7 @@ const OpInfo* find_op(const char* shader) {
 
 // The reference shaders' compile-time constants.
 constexpr float kRefEps = 1e-5f;   // shader/RmsNorm-GEMV-FP16.comp:18
+constexpr float kRefEpsRms = 1e-5f;  // shader/RmsNorm.comp:9
 constexpr int kRefDModel = 4096;   // shader/RmsNorm-GEMV-FP16.comp:8
 
 void need_bytes(const operation& op, int idx, int64_t bytes, const char* what) {
@@ -265,6 +283,19 @@ const void* dptr(const operation& op, int idx) { return op.buffers[idx].buffer; 
 void run_op(Ctx* c, const operation& op) {
     const OpInfo* info = find_op(op.shader);
     if (!info) fatal("unknown operator (shader) name: %s", op.shader);
+    if (info->kind == kOpRmsNorm) {
+        // No push constants: one workgroup per row of 256 (shader/RmsNorm.comp:5,22-23)
+        constexpr int kWidth = 256;
+        const int rows = op.dispatchX;
+        if (rows <= 0) fatal("%s: dispatchX=%d rows must be positive", op.shader, rows);
+        if (op.bufferCount < 2) fatal("%s: expects 2 bindings, got %d", op.shader, op.bufferCount);
+        need_bytes(op, 0, 4LL * kWidth * rows, "x");
+        need_bytes(op, 1, 4LL * kWidth, "gamma");
+        const int rc = vkc_rmsnorm_rows((float*)dptr(op, 0), (const float*)dptr(op, 1), rows, kWidth, kRefEpsRms,
+                                        c->stream);
+        if (rc != 0) fatal("%s: %s", op.shader, vkc_last_error());
+        return;
+    }
     if (op.pushConstantCount < 3 || op.pushConstantCount > MAX_PUSH_CONSTANTS)
         fatal("%s: expected at least 3 push constants {M, N, K}, got %d", op.shader,
               op.pushConstantCount);
@@ -386,6 +417,19 @@ void run_op(Ctx* c, const operation& op) {
             need_bytes(op, 3, 4LL * N, "y");
             rc = vkc_attention_decode(dptr(op, 2), 16, dptr(op, 0), dptr(op, 1), (float*)dptr(op, 3),
                                       n_q, n_kv, hd, ctxlen, scale, nullptr, 0, c->stream);
+            break;
+        }
+        case kOpRmsNorm:  // handled above (no push constants)
+            break;
+        case kOpGemvRowMajor:
+        case kOpGemvSquare: {
+            const int n = info->kind == kOpGemvSquare ? K : N;
+            need_count(3);
+            need_bytes(op, 0, 4LL * K, "x");
+            need_bytes(op, 1, 4LL * K * n, "W");
+            need_bytes(op, 2, 4LL * n, "y");
+            rc = vkc_gemv_rowmajor((const float*)dptr(op, 1), (const float*)dptr(op, 0), (float*)dptr(op, 2), n, K,
+                                   c->stream);
             break;
         }
         case kOpGemm: {

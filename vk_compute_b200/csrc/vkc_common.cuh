@@ -32,12 +32,18 @@ int set_error(int code, const char* fmt, ...);
 // Programmatic dependent launch switch shared by all launchers.
 bool pdl_enabled();
 
-// Library-owned scratch of the current device: at least `bytes`, zero-filled
-// when (re)allocated.  Kernels that use it leave their ticket words at zero,
-// so consecutive launches on one stream may share it; launches that overlap
-// on different streams must not.  Words [0, 64) are reserved for the status
-// word written by bounded device waits.
-int device_workspace(size_t bytes, void** out, cudaStream_t stream);
+// Library-owned scratch of the current device, one allocation per user (the
+// operators that keep state between calls in it must not share one): at
+// least `bytes`, zero-filled when (re)allocated.  Kernels that use it leave
+// their ticket words at zero, so consecutive launches on one stream may share
+// it; launches that overlap on different streams must not.  Words [0, 64) are
+// reserved for the status word written by bounded device waits.
+enum : int {
+    kWorkspaceAttention = 0,  // split partials and merge tickets of decode attention
+    kWorkspaceRowGemv = 1,    // K-slice partials of the row-major GEMV
+    kWorkspaceUsers = 2,
+};
+int device_workspace(size_t bytes, void** out, cudaStream_t stream, int user);
 constexpr size_t kWorkspaceHeader = 256;
 
 // Fills the launch attributes every kernel launcher uses: an optional cluster

@@ -15,6 +15,12 @@ ships these operators as separate shaders and no driver chains them
 RmsNorm-swiglu-ffn-*.comp); the chain, the KV append and the residual adds are
 this library's.
 
+The model's fused QKV matrix has its output rows in the order
+[Q heads | K0 V0 | K1 V1 | ...]: each KV head's K rows followed by its V rows.
+With head_dim 128 a K/V pair is exactly one 256-row scale block, so every
+shard below is made of whole scale blocks of the unsharded matrix and the
+quantised model is the same at 1, 2, 4 and 8 GPUs.
+
 Sharding over `world` GPUs of one node (one process each), two exchanges per
 layer: rank r owns query heads [r*nq/world, (r+1)*nq/world) and the matching
 KV heads, so QKV (split by output rows, head-aligned), RoPE, the cache and
@@ -70,7 +76,7 @@ class ShardPlan:
     world: int
     q_heads: tuple[int, int]     # [lo, hi) query heads
     kv_heads: tuple[int, int]    # [lo, hi) KV heads
-    qkv_cols: tuple[int, ...]    # output rows of the full QKV matrix, shard order [Q | K | V]
+    qkv_cols: tuple[int, ...]    # output rows of the full QKV matrix, shard order [Q | K0 V0 | ...]
     o_k: tuple[int, int]         # [lo, hi) of the O projection's input (the rank's heads x head_dim)
     ffn_rows: tuple[int, int]    # [lo, hi) of inter: gate/up outputs, down inputs
 
@@ -96,13 +102,14 @@ def shard_plan(cfg: DecoderConfig, rank: int, world: int) -> ShardPlan:
     nq, nkv = cfg.n_q // world, cfg.n_kv // world
     q0, k0 = rank * nq, rank * nkv
     q_cols = range(q0 * hd, (q0 + nq) * hd)
-    k_cols = range(cfg.n_q * hd + k0 * hd, cfg.n_q * hd + (k0 + nkv) * hd)
-    v_cols = range((cfg.n_q + cfg.n_kv) * hd + k0 * hd, (cfg.n_q + cfg.n_kv) * hd + (k0 + nkv) * hd)
+    kv_cols = range(cfg.n_q * hd + 2 * k0 * hd, cfg.n_q * hd + 2 * (k0 + nkv) * hd)  # K/V pairs of its heads
     f = cfg.inter // world
-    plan = ShardPlan(rank, world, (q0, q0 + nq), (k0, k0 + nkv), tuple(q_cols) + tuple(k_cols) + tuple(v_cols),
+    plan = ShardPlan(rank, world, (q0, q0 + nq), (k0, k0 + nkv), tuple(q_cols) + tuple(kv_cols),
                      (q0 * hd, (q0 + nq) * hd), (rank * f, (rank + 1) * f))
     if cfg.bits <= 8:
-        for n in (len(plan.qkv_cols), f):
+        # both row ranges of the QKV shard, and the gate/up shard, start and
+        # end on 256-row scale blocks of the unsharded matrices
+        for n in (cfg.n_q * hd, nq * hd, 2 * nkv * hd, f):
             if n % 256:
                 raise ValueError(f"a {cfg.bits}-bit shard of {n} rows is not a whole number of 256-row scale blocks")
     kpc = 128 // cfg.bits
@@ -143,9 +150,9 @@ def _pack(w: torch.Tensor, bits: int) -> ops.PackedWeight:
 def build_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: int = 0) -> LayerShard:
     """Random-init weights of one layer, this rank's shard.  Every rank draws
     the same full matrices from the same seeds and keeps its own part (QKV
-    and gate/up: output rows; O and down: input rows), so the sharded model
-    equals the unsharded one (for int4/int8, up to the QKV shard's scale
-    blocks: its head-permuted rows group into other 256-row blocks)."""
+    and gate/up: output rows; O and down: input rows).  Every part is made of
+    whole 256-row scale blocks of the full matrix (shard_plan checks it), so
+    the sharded model equals the unsharded one, quantisation included."""
     base = seed * 1000 + layer * 10
     H, I = cfg.hidden, cfg.inter
     cols = torch.tensor(plan.qkv_cols, device=device)
@@ -269,7 +276,7 @@ class ShardedDecoder:
             base, peer_in = (b.x_mid, self._in_d) if fused and li > 0 else (b.x, None)
             ops.qkv_rope_append(L.qkv, base, L.g_attn, self.theta, pos, head_dim=hd, q_rows=q_rows, kv_rows=kv_rows,
                                 kcache=L.kcache, vcache=L.vcache, ctx_cap=cfg.ctx, eps=cfg.eps, out=b.qkv,
-                                peer=peer_in)
+                                peer=peer_in, kv_layout="interleaved")
             ops.attention_decode(b.qkv[:q_rows], L.kcache, L.vcache, p.n_q, p.n_kv, hd, pos + 1, scale,
                                  workspace=b.ws, out=b.attn, ctx_cap=cfg.ctx, after_append=True)
             if single:

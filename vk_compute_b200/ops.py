@@ -175,20 +175,27 @@ def gemv_peer(w: PackedWeight, x: torch.Tensor, slots: torch.Tensor, rank: int, 
                               w.K, _s(stream)))
 
 
+KV_LAYOUTS = {"split": 0, "interleaved": 1}
+
+
 def qkv_rope_append(w: PackedWeight, x, gamma, theta, pos: int, *, head_dim: int, q_rows: int, kv_rows: int,
                     kcache: torch.Tensor, vcache: torch.Tensor, ctx_cap: int, eps: float = 1e-6,
-                    rms_dim: int | None = None, out=None, stream=None, peer: PeerInput | None = None) -> torch.Tensor:
+                    rms_dim: int | None = None, out=None, stream=None, peer: PeerInput | None = None,
+                    kv_layout: str = "split") -> torch.Tensor:
     """Fused QKV projection + RoPE + KV-cache append at token `pos`; with
-    `peer`, the input is x (the base) plus the peer exchange's slots."""
+    `peer`, the input is x (the base) plus the peer exchange's slots.  The
+    rows after Q are [K heads | V heads] ("split") or [K0 V0 | K1 V1 | ...]
+    ("interleaved")."""
     y = _out(w.N, x, out)
+    lay = KV_LAYOUTS[kv_layout]
     if peer is None:
         check(lib().vkc_rmsnorm_gemv_rope_kv(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x), _p(gamma),
                                              _p(theta), _p(y), w.N, w.K, eps, rms_dim or w.K, pos, head_dim, q_rows,
-                                             kv_rows, _p(kcache), _p(vcache), ctx_cap, _s(stream)))
+                                             kv_rows, lay, _p(kcache), _p(vcache), ctx_cap, _s(stream)))
     else:
         check(lib().vkc_rmsnorm_gemv_rope_kv_peer(w.bits, _p(w.packed), _p(w.scale), _p(w.zero), _p(x),
                                                   C.addressof(peer), _p(gamma), _p(theta), _p(y), w.N, w.K, eps,
-                                                  rms_dim or w.K, pos, head_dim, q_rows, kv_rows, _p(kcache),
+                                                  rms_dim or w.K, pos, head_dim, q_rows, kv_rows, lay, _p(kcache),
                                                   _p(vcache), ctx_cap, _s(stream)))
     return y
 
@@ -256,6 +263,23 @@ def attention_decode(q, kcache, vcache, n_q: int, n_kv: int, head_dim: int, ctx:
     return o
 
 
+def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, stream=None) -> torch.Tensor:
+    """In-place RMSNorm of each row of x ([rows][width] fp32) with gamma[width]
+    (shader/RmsNorm.comp with width 256)."""
+    rows, width = x.shape
+    check(lib().vkc_rmsnorm_rows(_p(x), _p(gamma), rows, width, eps, _s(stream)))
+    return x
+
+
+def gemv_rowmajor(w: torch.Tensor, x: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    """y = W^T x for a plain row-major K x N fp32 matrix (shader/gemv2.comp,
+    gemv3.comp; gemv1.comp for square W)."""
+    K, N = w.shape
+    y = _out(N, x, out)
+    check(lib().vkc_gemv_rowmajor(_p(w), _p(x), _p(y), N, K, _s(stream)))
+    return y
+
+
 def gemm_f32(a: torch.Tensor, b: torch.Tensor, out=None, stream=None) -> torch.Tensor:
     M, K = a.shape
     K2, N = b.shape
@@ -294,9 +318,26 @@ def get_pdl() -> bool:
     return bool(lib().vkc_get_pdl())
 
 
+GEMV_PLANS = {"auto": 0, "cluster": 1, "per-sm": 2, "per-sm-half": 3}
+
+
+def set_gemv_plan(plan: str) -> None:
+    """Kernel of the single-vector GEMV family (vkc_set_gemv_plan): "auto"
+    chooses per shape, "cluster" always splits K across a cluster, "per-sm"
+    runs one CTA per SM with whole-K column ranges wherever it can (a 1024-
+    thread CTA owning the SM), "per-sm-half" the same with a 512-thread CTA
+    that leaves half the SM to the next launch."""
+    check(lib().vkc_set_gemv_plan(GEMV_PLANS[plan]))
+
+
+def get_gemv_plan() -> str:
+    v = lib().vkc_get_gemv_plan()
+    return next(k for k, n in GEMV_PLANS.items() if n == v)
+
+
 def device_status(clear: bool = False) -> int:
-    """Status word of the current device (waits for it): bit 1 producer, 2
-    consumer, 4 cluster reduction, 8 peer-exchange wait ran out."""
+    """Status word of the current device (waits for it); flags 0x1 producer,
+    0x2 consumer, 0x4 cluster reduction, 0x8 peer-exchange wait ran out."""
     v = C.c_uint(0)
     check(lib().vkc_device_status(C.byref(v), int(clear)))
     return int(v.value)
