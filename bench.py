@@ -753,9 +753,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true", help="launch steps eagerly instead of from a CUDA graph")
     ap.add_argument("--no-pdl", action="store_true", help="plain launches (no programmatic dependent launch)")
-    ap.add_argument("--gemv-plan", default="auto", choices=["auto", "cluster", "per-sm", "per-sm-half"],
+    ap.add_argument("--gemv-plan", default="auto", choices=["auto", "cluster", "per-sm", "per-sm-half", "auto-full"],
                     help="single-vector GEMV kernel: chosen per shape, cluster split-K, or one CTA per SM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv-fma", action="store_true",
+                    help="8/4-bit weights on the per-SM GEMV with fp32 FMAs instead of integer dot products")
+    ap.add_argument("--attention-plan", default="auto", choices=["auto", "clustered", "per-sm"],
+                    help="decode attention: chosen per shape, clusters of 8 CTAs per KV head, or one CTA per SM")
     ap.add_argument("--no-decode", action="store_true", help="skip the 36-layer decode-step measurement")
     ap.add_argument("--no-decode-parity", action="store_true",
                     help="skip the N>1 decode-step check against the same model on one GPU")
@@ -787,6 +791,8 @@ def main():
 
     ops.set_pdl(not args.no_pdl)
     ops.set_gemv_plan(args.gemv_plan)
+    ops.set_gemv_int_dot(not args.gemv_fma)
+    ops.set_attention_plan(args.attention_plan)
     wl = build_workload(args.workload, rank, device, world)
     step = wl["step"]
     scaling = wl.get("scaling", "weak")
@@ -880,6 +886,7 @@ def main():
         e2e = {"value": round(world * wl["bytes"] / dt / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": r["h2d_bytes_per_step"], "d2h_bytes_per_step": r["d2h_bytes_per_step"],
                "us_per_step": round(dt * 1e6, 2),
+               "host_us_per_call": {k: r.get("us_" + k) for k in ("write", "execute", "read")},
                "path": "C host (vkc_e2e_bench): writeBuffer + execute + readBuffer per step, reference ABI, "
                        "host wall clock, weight pool > 4x L2; execute timing events off (vkc_set_timing(0): "
                        "the program never calls getExecutionTime)"}
@@ -942,7 +949,8 @@ def main():
             "config": {"workload": args.workload, "description": WORKLOADS[args.workload],
                        "bytes_per_step": job_bytes, "bytes_per_rank_step": bytes_rank, "per_rank": meta,
                        "l2": "rotating weight pool >= 4x L2; each step reads weights last touched a full pool ago",
-                       "graph": not args.no_graph, "pdl": not args.no_pdl, "gemv_plan": args.gemv_plan,
+                       "graph": not args.no_graph, "pdl": not args.no_pdl, "gemv_plan": args.gemv_plan, "gemv_int_dot": not args.gemv_fma,
+                       "attention_plan": args.attention_plan,
                        "parallelism": parallelism},
             "frac_of_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 2),

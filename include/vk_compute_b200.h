@@ -60,9 +60,22 @@ int vkc_get_timing(void);
  * K and reduce in distributed shared memory.  1 always uses the cluster
  * kernel; 2 uses the one-CTA-per-SM kernel with 1024-thread CTAs wherever it
  * can run, 3 with 512-thread CTAs that leave half of each SM to the next
- * launch.  Results agree to rounding.  No counterpart in the reference. */
+ * launch, 4 chooses per shape like 0 but with 1024-thread CTAs (for chains
+ * whose other kernels need more than half of each SM).  The setting belongs to the calling host thread.  Results agree to
+ * rounding.  No counterpart in the reference. */
 int vkc_set_gemv_plan(int plan);
 int vkc_get_gemv_plan(void);
+/* Arithmetic of 8/4-bit weights on the one-CTA-per-SM kernel, for the calling
+ * host thread.  1 (default): integer dot products -- each chunk row's folded
+ * activations x*gamma*scale become 16-bit integers against the row's largest
+ * magnitude (steps of 2^-15 of it), every code-times-activation sum is exact
+ * in 32-bit integers (dp4a), and each row's sum is scaled once into an fp32
+ * accumulator; about a third of the instructions per weight of 0.  0: fp32
+ * fused multiply-adds on the exactly converted codes.  Dequantisation is
+ * q*scale - zero either way; the two agree to about 1e-5 relative.  No
+ * counterpart in the reference. */
+void vkc_set_gemv_int_dot(int enable);
+int vkc_get_gemv_int_dot(void);
 /* 1 if `shader` ("GEMV-INT4.spv", ...) names an operator execute() runs. */
 int vkc_has_operator(const char* shader);
 /* Waits for the current device and returns its status word, whose flags
@@ -201,6 +214,15 @@ int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const 
  * (calls on different streams must then not overlap), or caller memory of
  * vkc_attention_workspace_bytes() bytes, zero-filled before its first use. */
 size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
+/* How decode attention splits the cache (head_dim 64 or 128), for the calling
+ * host thread: 0 (default) chooses per shape; 1 clusters of 8 CTAs per KV
+ * head merging in distributed shared memory, two CTAs per SM; 2 at most one
+ * CTA per SM, each streaming a long token range through a deep ring, the
+ * splits of a head merged by the last to finish.  The workspace size
+ * (vkc_attention_workspace_bytes) depends on the plan in force.  No
+ * counterpart in the reference. */
+int vkc_set_attention_plan(int plan);
+int vkc_get_attention_plan(void);
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                          void* workspace, size_t workspace_bytes, void* stream);
@@ -290,7 +312,7 @@ int vkc_ipc_free(void* ptr);
  * . W[N][K]^T (bf16); A and W row-major, so W is the K-major (N rows of K)
  * layout of a linear layer's weight.  The batched form of gemm.comp's
  * contraction (shader/gemm.comp:19-59) for prefill.  K a multiple of 64, N a
- * multiple of 96, any M (tiles of 128 rows).  Pointers 16-byte aligned. */
+ * multiple of 16, any M (tiles of 128 rows).  Pointers 16-byte aligned. */
 int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, void* stream);
 /* Status flags of vkc_gemm_bf16 on the current device (0x10: a bounded wait
  * ran out); waits for the device; `clear` resets them. */
@@ -311,6 +333,40 @@ int vkc_quantize(const float* w, int K, int N, int bits, int symmetric, int fp16
 /* transpose_block16 (src/data.c:198-222) on the device: `in` is K x N
  * row-major (fp32, fp16, u8, or u4 two per byte). */
 int vkc_pack_block16(const void* in, void* out, int K, int N, int bits, void* stream);
+
+/* ---- weights on disk (no counterpart in the reference, which builds its
+ * matrices in memory with src/data.c and keeps no model files) ----
+ * A file holds named matrices in exactly the device layout above: the
+ * transpose_block16 chunks and, for 8/4-bit weights, block-major fp32 scale
+ * and zero, each section 256-byte aligned (format: csrc/weights_file.cu).
+ * Loading copies each section from disk through pinned memory to the device
+ * with no repacking.  Errors (unreadable, truncated or inconsistent files,
+ * unknown shapes) return VKC_ERR_ARG with a message. */
+typedef struct vkc_weight_entry {
+    char name[64];       /* NUL-terminated */
+    int bits, K, N;      /* 32, 16, 8 or 4; y = W^T x with W K x N */
+    const void* data;    /* write: host packed chunks, K*N*bits/8 bytes */
+    const float* scale;  /* write: host [N/256][K] (8/4-bit only) */
+    const float* zero;
+} vkc_weight_entry;
+typedef struct vkc_weight_file vkc_weight_file;
+
+/* Writes `count` matrices (host memory) to `path`. */
+int vkc_weights_write(const char* path, const vkc_weight_entry* entries, int count);
+/* Opens and validates a file; vkc_weights_close releases it. */
+int vkc_weights_open(const char* path, vkc_weight_file** file);
+int vkc_weights_count(const vkc_weight_file* file);
+/* Index of the matrix called `name`, or -1. */
+int vkc_weights_find(const vkc_weight_file* file, const char* name);
+/* Name and shape of matrix `index` (the pointers of *info are set to NULL). */
+int vkc_weights_info(const vkc_weight_file* file, int index, vkc_weight_entry* info);
+/* Matrix `index` into device memory (data: K*N*bits/8 bytes; scale, zero:
+ * K*N/256 floats each, ignored for 16/32-bit) through pinned host memory;
+ * returns once the copies on `stream` are done. */
+int vkc_weights_read(vkc_weight_file* file, int index, void* data, float* scale, float* zero, void* stream);
+/* The same into host memory. */
+int vkc_weights_read_host(vkc_weight_file* file, int index, void* data, float* scale, float* zero);
+void vkc_weights_close(vkc_weight_file* file);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,16 @@ from vk_compute_b200 import ops
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["clustered", "per-sm"])
+def attention_plan(request):
+    """Every case runs under both splits of the cache for the token-slice
+    kernel (head_dim 64/128): clusters of 8 CTAs per KV head, and at most one
+    CTA per SM with a deep ring; other head sizes ignore the plan."""
+    ops.set_attention_plan(request.param)
+    yield request.param
+    ops.set_attention_plan("auto")
+
+
 def make_cache(n_q, n_kv, hd, ctx, seed=0, scale=1.0):
     g = torch.Generator().manual_seed(seed)
     q = (torch.randn(n_q * hd, generator=g) * scale).half()

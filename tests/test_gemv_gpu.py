@@ -18,15 +18,19 @@ from vk_compute_b200 import ops
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["cluster", "per-sm", "per-sm-half"])
+@pytest.fixture(autouse=True, params=["cluster", "per-sm", "per-sm-half", "per-sm-fma"])
 def gemv_plan(request):
     """Every case runs on each single-vector kernel: clusters splitting K, and
     one CTA per SM with whole-K column ranges in its full-SM (1024 threads)
-    and half-SM (512 threads) shapes, wherever those can run; the automatic
-    choice picks one of them per shape."""
-    ops.set_gemv_plan(request.param)
+    and half-SM (512 threads) shapes, wherever those can run -- 8/4-bit
+    weights there with integer dot products, and ("per-sm-fma") with fp32
+    FMAs; the automatic choice picks one of them per shape."""
+    plan = "per-sm-half" if request.param == "per-sm-fma" else request.param
+    ops.set_gemv_plan(plan)
+    ops.set_gemv_int_dot(request.param != "per-sm-fma")
     yield request.param
     ops.set_gemv_plan("auto")
+    ops.set_gemv_int_dot(True)
 
 BITS = [32, 16, 8, 4]
 

@@ -26,6 +26,10 @@ SIGNATURES = {
     "vkc_device_status": (_i, [C.POINTER(C.c_uint), _i]),
     "vkc_wait_limits": (None, [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "vkc_set_gemv_plan": (_i, [_i]),
+    "vkc_set_gemv_int_dot": (None, [_i]),
+    "vkc_get_gemv_int_dot": (_i, []),
+    "vkc_set_attention_plan": (_i, [_i]),
+    "vkc_get_attention_plan": (_i, []),
     "vkc_get_gemv_plan": (_i, []),
     "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),
     "vkc_rmsnorm_gemv": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
@@ -59,6 +63,24 @@ SIGNATURES = {
                                            _p, _p, _i, _p]),
     "vkc_rmsnorm_swiglu_peer": (_i, [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _i, _p]),
 }
+
+
+class WeightEntry(C.Structure):
+    """vkc_weight_entry (include/vk_compute_b200.h)."""
+    _fields_ = [("name", C.c_char * 64), ("bits", C.c_int), ("K", C.c_int), ("N", C.c_int),
+                ("data", C.c_void_p), ("scale", C.c_void_p), ("zero", C.c_void_p)]
+
+
+SIGNATURES.update({
+    "vkc_weights_write": (_i, [C.c_char_p, C.POINTER(WeightEntry), _i]),
+    "vkc_weights_open": (_i, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "vkc_weights_count": (_i, [_p]),
+    "vkc_weights_find": (_i, [_p, C.c_char_p]),
+    "vkc_weights_info": (_i, [_p, _i, C.POINTER(WeightEntry)]),
+    "vkc_weights_read": (_i, [_p, _i, _p, _p, _p, _p]),
+    "vkc_weights_read_host": (_i, [_p, _i, _p, _p, _p]),
+    "vkc_weights_close": (None, [_p]),
+})
 
 
 class VkcError(RuntimeError):

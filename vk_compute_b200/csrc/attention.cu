@@ -790,8 +790,14 @@ __global__ void __launch_bounds__(kAttThreads, 2) attention_mma_kernel(const Att
 // only at the two ring barriers per sub-tile.  q and p are fp32 values split
 // into fp16 high and low parts, both multiplied (about 22 significant bits).
 // The four warp states are merged through shared memory at the end.
+//
+// Two shapes.  Clustered: ST = 3 ring stages, CL = 8 consecutive splits of a
+// KV head per cluster merging over DSMEM, two CTAs per SM.  Per-SM: ST = 6
+// stages (192 KB of the cache in flight per SM), CL = 1, one CTA per SM with
+// a long token range, the splits of a head merged by the last to finish.
 constexpr int kFaThreads = 128;
-constexpr int kFaCluster = 8;  // CTAs per cluster (consecutive splits of one KV head)
+constexpr int kFaCluster = 8;  // CTAs per cluster of the clustered shape
+constexpr int kFaDeepStages = 6;
 
 __device__ __forceinline__ void mma16816_full(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -806,8 +812,8 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     return y;
 }
 
-template <int G, int HD>
-__global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnParams p) {
+template <int G, int HD, int ST, int CL>
+__global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kernel(const AttnParams p) {
     using Geo = MmaGeo<HD>;
     constexpr int CH = Geo::CH, TT = Geo::TT, KROW = Geo::KROW, VROW = Geo::VROW, KU = Geo::KU, SU = Geo::SU;
     constexpr int NW = kFaThreads / 32;    // warps
@@ -828,7 +834,8 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
     const int nsub = (T + TT - 1) / TT;
     const int h0 = kv * G;
     uint4* ring = reinterpret_cast<uint4*>(smem);
-    uint4* qf = reinterpret_cast<uint4*>(smem + Geo::ring_bytes);  // [KS][32]
+    constexpr size_t kRingBytes = static_cast<size_t>(ST) * SU * 16;
+    uint4* qf = reinterpret_cast<uint4*>(smem + kRingBytes);  // [KS][32]
 
     pdl_launch_dependents();
 
@@ -842,7 +849,7 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
     const size_t v_step = static_cast<size_t>(kFaThreads / TT) * p.ctx_cap;
     const int k_dst0 = k_tok * KROW + k_chk, v_dst0 = KU + v_chk * VROW + v_tok;
     auto issue = [&](int s) {
-        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const uint32_t base = smem_addr(ring + (s % ST) * SU);
         const int nt = min(TT, T - s * TT);
         const size_t tok = static_cast<size_t>(s) * TT;
 #pragma unroll
@@ -863,13 +870,13 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
     // in flight writes) are requested before the wait on the previous kernel;
     // the rest, and q, after it.  Commit groups stay in sub-tile order.
     int s_pre = 0;
-    while (s_pre < kAttStages && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable) {
+    while (s_pre < ST && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable) {
         issue(s_pre);
         cp_commit();
         ++s_pre;
     }
     pdl_wait();
-    for (int s = s_pre; s < kAttStages; ++s) {
+    for (int s = s_pre; s < ST; ++s) {
         if (s < nsub) issue(s);
         cp_commit();
     }
@@ -909,9 +916,9 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
         for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
 
     for (int s = 0; s < nsub; ++s) {
-        cp_wait<kAttStages - 1>();
+        cp_wait<ST - 1>();
         __syncthreads();  // sub-tile s landed for all threads (and q fragments, first time)
-        const uint32_t base = smem_addr(ring + (s % kAttStages) * SU);
+        const uint32_t base = smem_addr(ring + (s % ST) * SU);
         const int nt = min(TT, T - s * TT);
 #pragma unroll
         for (int sl = 0; sl < SPW; ++sl) {
@@ -986,7 +993,7 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
             }
         }
         __syncthreads();  // slot of sub-tile s consumed by all warps
-        if (s + kAttStages < nsub) issue(s + kAttStages);
+        if (s + ST < nsub) issue(s + ST);
         cp_commit();
     }
     cp_wait<0>();
@@ -1052,7 +1059,7 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
         crec[tid * RP + HD + 1] = L;
     }
 
-    // ---- cluster of kFaCluster consecutive splits: rank 0 merges the records
+    // ---- cluster of CL consecutive splits: rank 0 merges the records
     // of its peers through distributed shared memory.  Barrier 1 publishes the
     // records; barrier 2 keeps the peers resident until rank 0 has read them.
     __syncthreads();
@@ -1069,13 +1076,13 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
     const uint32_t crec_addr = smem_addr(crec);
     // Four dimensions per thread: the (m, l) and values of every rank are
     // loaded in one round, then summed in rank order.
-    const int nc = p.splits / kFaCluster, cidx = split / kFaCluster;
+    const int nc = p.splits / CL, cidx = split / CL;
     for (int qd = tid; qd < G * HD / 4; qd += kFaThreads) {
         const int g = (qd * 4) / HD, d = qd * 4 - g * HD;
-        float4 v[kFaCluster];
-        float2 ml[kFaCluster];
+        float4 v[CL];
+        float2 ml[CL];
 #pragma unroll
-        for (int r = 0; r < kFaCluster; ++r) {
+        for (int r = 0; r < CL; ++r) {
             const uint32_t ra = map_cluster_addr(crec_addr + (g * RP + d) * 4, r);
             const uint32_t rs = map_cluster_addr(crec_addr + (g * RP + HD) * 4, r);
             asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
@@ -1086,11 +1093,11 @@ __global__ void __launch_bounds__(kFaThreads, 2) attention_fa_kernel(const AttnP
         }
         float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < kFaCluster; ++r) M = fmaxf(M, ml[r].x);
+        for (int r = 0; r < CL; ++r) M = fmaxf(M, ml[r].x);
         float L = 0.f;
         float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int r = 0; r < kFaCluster; ++r) {
+        for (int r = 0; r < CL; ++r) {
             const float w = ml[r].x == -INFINITY ? 0.f : exp2f(ml[r].x - M);
             L = fmaf(w, ml[r].y, L);
             acc4.x = fmaf(w, v[r].x, acc4.x);
@@ -1137,7 +1144,24 @@ struct AttnPlan {
     int splits;   // CTAs per KV head (grid x)
     int tpc;      // tokens per CTA (a multiple of 16)
     int records;  // partial records per query head in the workspace
+    bool per_sm;  // token-slice kernel in its per-SM shape (deep ring, no clusters)
 };
+
+// Attention plan (vkc_set_attention_plan), per host thread: 0 chooses per
+// shape, 1 the clustered token-slice shape, 2 the per-SM shape.
+thread_local int g_attn_plan = 0;
+
+int current_sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
 
 // Splits: about two CTAs per SM (148 SMs), but at least three sub-tiles
 // (~96 KB of cache) per CTA, so a small cache (a shard with one KV head) is
@@ -1174,12 +1198,32 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
     int t = (ctx + target - 1) / target;
     t = ((t + 15) / 16) * 16;
     pl.tpc = t;
+    pl.per_sm = false;
     if (pl.kind == AttnPlan::kSlice) {
         pl.splits = target;
         pl.records = target / kFaCluster;
     } else {
         pl.splits = (ctx + t - 1) / t;
         pl.records = pl.splits;
+    }
+    if (pl.kind == AttnPlan::kSlice && g_attn_plan != 1) {
+        // Per-SM shape: at most one CTA per SM over all KV heads, each with at
+        // least two sub-tiles, its range streamed through the deep ring; the
+        // splits of a head merge through the workspace.
+        const int tt = 8192 / hd;
+        const int per_head = current_sm_count() / n_kv > 0 ? current_sm_count() / n_kv : 1;
+        int tpc = (ctx + per_head - 1) / per_head;
+        tpc = ((tpc + 15) / 16) * 16;
+        if (tpc < 2 * tt) tpc = 2 * tt;
+        const int splits = (ctx + tpc - 1) / tpc;
+        // automatic choice: the per-SM shape when it gives every CTA at least
+        // two sub-tiles and keeps the grid in one wave
+        if (g_attn_plan == 2 || splits * n_kv <= current_sm_count()) {
+            pl.per_sm = true;
+            pl.tpc = tpc;
+            pl.splits = splits;
+            pl.records = splits;
+        }
     }
     return pl;
 }
@@ -1241,7 +1285,7 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
-    cfg.numAttrs = launch_attrs(attrs, pl.kind == AttnPlan::kSlice ? kFaCluster : 1);
+    cfg.numAttrs = launch_attrs(attrs, pl.kind == AttnPlan::kSlice && !pl.per_sm ? kFaCluster : 1);
     auto go = [&](auto kern, size_t smem) -> int {
         if (merge_min > smem) smem = merge_min;
         cfg.dynamicSmemBytes = smem;
@@ -1253,13 +1297,23 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
     if (pl.kind == AttnPlan::kSlice) {
         auto pick = [&](auto hd_tag) -> int {
             constexpr int HD = decltype(hd_tag)::value;
-            const size_t smem = MmaGeo<HD>::ring_bytes + MmaGeo<HD>::q_bytes;
             cfg.blockDim = dim3(kFaThreads, 1, 1);
+            if (pl.per_sm) {
+                constexpr int ST = kFaDeepStages;
+                const size_t smem = static_cast<size_t>(ST) * MmaGeo<HD>::SU * 16 + MmaGeo<HD>::q_bytes;
+                switch (G) {
+                    case 1: return go(attention_fa_kernel<1, HD, ST, 1>, smem);
+                    case 2: return go(attention_fa_kernel<2, HD, ST, 1>, smem);
+                    case 4: return go(attention_fa_kernel<4, HD, ST, 1>, smem);
+                    default: return go(attention_fa_kernel<8, HD, ST, 1>, smem);
+                }
+            }
+            const size_t smem = MmaGeo<HD>::ring_bytes + MmaGeo<HD>::q_bytes;
             switch (G) {
-                case 1: return go(attention_fa_kernel<1, HD>, smem);
-                case 2: return go(attention_fa_kernel<2, HD>, smem);
-                case 4: return go(attention_fa_kernel<4, HD>, smem);
-                default: return go(attention_fa_kernel<8, HD>, smem);
+                case 1: return go(attention_fa_kernel<1, HD, kAttStages, kFaCluster>, smem);
+                case 2: return go(attention_fa_kernel<2, HD, kAttStages, kFaCluster>, smem);
+                case 4: return go(attention_fa_kernel<4, HD, kAttStages, kFaCluster>, smem);
+                default: return go(attention_fa_kernel<8, HD, kAttStages, kFaCluster>, smem);
             }
         };
         if (hd == 64) return pick(std::integral_constant<int, 64>());
@@ -1295,6 +1349,13 @@ extern "C" {
 size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx) {
     return attention_workspace_bytes(n_q, n_kv, head_dim, ctx);
 }
+
+int vkc_set_attention_plan(int plan) {
+    if (plan < 0 || plan > 2) return set_error(kErrArg, "attention plan %d (expected 0, 1 or 2)", plan);
+    g_attn_plan = plan;
+    return kOk;
+}
+int vkc_get_attention_plan(void) { return g_attn_plan; }
 
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,

@@ -8,7 +8,8 @@
  *   op: RmsNorm-GEMV-INT8 | GEMV-FP16
  * The program never asks for getExecutionTime, so it turns execute()'s timing
  * events off (vkc_set_timing(0)), as such a program would.
- * Prints one JSON object: us_per_step, h2d_bytes_per_step, d2h_bytes_per_step. */
+ * Prints one JSON object: us_per_step, h2d_bytes_per_step, d2h_bytes_per_step,
+ * and the host time of each call (write / execute / read, us per step). */
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -105,18 +106,27 @@ int main(int argc, char** argv) {
         execute(s, &ops[i % pool], 1);
         readBuffer(s.dev.device, s.dev.physicalDevice, s.dev.queue, yb, hy);
     }
+    double t_write = 0, t_exec = 0, t_read = 0;
     const double t0 = now_us();
     for (int i = 0; i < steps; ++i) {
+        const double a = now_us();
         writeBuffer(s.dev.device, s.dev.queue, xb, hx);
+        const double b = now_us();
         execute(s, &ops[(warmup + i) % pool], 1);
+        const double c = now_us();
         readBuffer(s.dev.device, s.dev.physicalDevice, s.dev.queue, yb, hy);
+        const double d = now_us();
+        t_write += b - a;
+        t_exec += c - b;
+        t_read += d - c;
     }
     const double us = (now_us() - t0) / steps;
     double check = 0;
     for (int i = 0; i < N; ++i) check += hy[i];
     printf("{\"us_per_step\": %.3f, \"h2d_bytes_per_step\": %d, \"d2h_bytes_per_step\": %d, \"pool\": %d, "
-           "\"steps\": %d, \"warmup\": %d, \"checksum\": %.6e}\n",
-           us, K * 4, N * 4, pool, steps, warmup, check);
+           "\"steps\": %d, \"warmup\": %d, \"checksum\": %.6e, \"us_write\": %.3f, \"us_execute\": %.3f, "
+           "\"us_read\": %.3f}\n",
+           us, K * 4, N * 4, pool, steps, warmup, check, t_write / steps, t_exec / steps, t_read / steps);
     for (int p = 0; p < pool; ++p)
         for (int j = 0; j < (int8 ? 3 : 1); ++j) destroyBuffer(s.dev.device, wbs[3 * p + j]);
     destroyBuffer(s.dev.device, xb);

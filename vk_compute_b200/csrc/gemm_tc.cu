@@ -7,15 +7,21 @@
 //
 // At M = 64 the product is bound by streaming W (100 MB) from HBM, not by the
 // tensor cores, so the kernel is a weight stream with the MMA in the loop:
-// - CTA n owns output columns [n BN, (n + 1) BN) for all rows of one 128-row
-//   M tile, and the whole K range: no split-K, no reduction.  BN = 96 puts
-//   12288 / 96 = 128 CTAs (one per SM) on the GPU.
+// - A CTA owns a range of output columns for all rows of one 128-row M tile,
+//   and the whole K range: no split-K, no reduction.  The columns are split
+//   in two widths 16 apart (each width with its own tensor map) over the
+//   fewest CTAs that keep the widest range as narrow as one CTA per SM
+//   allows: 12288 columns go to 128 CTAs of 96 (148 CTAs would still need
+//   ranges of 96, and measured slower).
 // - TMA (cp.async.bulk.tensor, 128-byte swizzle) loads K tiles of 64 into a
-//   ring of kStages shared-memory stages: the A tile (128 rows; rows past M are
-//   zero-filled by TMA) and the W tile (BN rows).  One thread produces.
-// - One thread issues tcgen05.mma kind::f16 (M = 128, N = BN, K = 16; bf16
-//   inputs, fp32 accumulator in TMEM), four per K tile, and returns each stage
-//   to the producer with tcgen05.commit on the stage's "empty" mbarrier.
+//   ring of kStages shared-memory stages: the A tile and the W tile.  With
+//   M <= 64 only A's 64 real rows are loaded; rows 64..127 of every stage are
+//   zeroed once, so the M = 128 MMA multiplies them as zeros without moving
+//   them again.  One thread produces.
+// - One thread issues tcgen05.mma kind::f16 (M = 128, N = the CTA's width,
+//   K = 16; bf16 inputs, fp32 accumulator in TMEM), four per K tile, and
+//   returns each stage to the producer with tcgen05.commit on the stage's
+//   "empty" mbarrier.
 // - After the last tile a commit signals the epilogue: the four warps read
 //   their 32 TMEM lanes (rows) with tcgen05.ld and store fp32 rows of C.
 // Every mbarrier wait is bounded; a timeout sets flag 0x10 of the status word and
@@ -35,14 +41,15 @@ constexpr int kStages = 6;
 constexpr int kTcThreads = 128;
 constexpr unsigned kStatusTcTimeout = 16u;
 
-template <int BN>
+constexpr int kBNMax = 128;  // widest CTA column range (the stage holds this many W rows)
+
 struct TcGeo {
     static constexpr int a_bytes = kBM * kBK * 2;  // 16 KB
-    static constexpr int b_bytes = BN * kBK * 2;
+    static constexpr int b_bytes = kBNMax * kBK * 2;
     static constexpr int stage_bytes = a_bytes + b_bytes;
-    static constexpr int tmem_cols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int tmem_cols = kBNMax;
     static constexpr size_t smem_bytes = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * stage_bytes + 256;
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M = 128 MMA needs N in [16, 256], a multiple of 16");
+    static_assert(kBNMax % 16 == 0 && kBNMax <= 256, "M = 128 MMA needs N in [16, 256], a multiple of 16");
     static_assert(a_bytes % 1024 == 0 && b_bytes % 1024 == 0, "stages stay 1024-byte aligned");
 };
 
@@ -85,9 +92,8 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
 }
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
 // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-template <int BN>
-__device__ __forceinline__ uint32_t idesc_bf16() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+__device__ __forceinline__ uint32_t idesc_bf16(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
            (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -106,11 +112,13 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-template <int BN>
+// CTAs [0, n_hi) own bn_lo + 16 columns (map_w_hi), the rest bn_lo (map_w_lo);
+// a_rows is the A box height (64 when M <= 64, else 128).
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, float* c,
-                   int M, int N, int K, unsigned* status) {
-    using Geo = TcGeo<BN>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w_lo,
+                   const __grid_constant__ CUtensorMap map_w_hi, float* c, int M, int N, int K, int n_hi, int bn_lo,
+                   int a_rows, unsigned* status) {
+    using Geo = TcGeo;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned stages (128-byte swizzle atoms), barriers after them.
     const uint32_t raw = smem_addr(smem_raw);
@@ -124,8 +132,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int cta = blockIdx.x;
+    const bool wide = cta < n_hi;
+    const int BN = wide ? bn_lo + 16 : bn_lo;
+    const int n0 = wide ? cta * BN : n_hi * (bn_lo + 16) + (cta - n_hi) * bn_lo;
+    const CUtensorMap* map_w = wide ? &map_w_hi : &map_w_lo;
+    const int m0 = blockIdx.y * kBM;
     const int KT = K / kBK;
+    const uint32_t a_load = static_cast<uint32_t>(a_rows) * kBK * 2;  // A bytes TMA writes per stage
+    const uint32_t stage_tx = a_load + static_cast<uint32_t>(BN) * kBK * 2;
+
+    // With a 64-row A box, rows 64..127 of every stage's A tile stay zero.
+    if (a_rows < kBM) {
+        for (int s = 0; s < kStages; ++s) {
+            uint4* z = reinterpret_cast<uint4*>(smem_raw + (base - raw) + s * Geo::stage_bytes + a_load);
+            for (int i = tid; i < static_cast<int>((Geo::a_bytes - a_load) / 16); i += kTcThreads)
+                z[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMA's reads
+    }
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -163,13 +188,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (s_abort) break;
             const uint32_t sa = base + s * Geo::stage_bytes;
-            mbar_expect_tx(full(s), Geo::stage_bytes);
+            mbar_expect_tx(full(s), stage_tx);
             tma_load_2d(sa, &map_a, kt * kBK, m0, full(s));
-            tma_load_2d(sa + Geo::a_bytes, &map_w, kt * kBK, n0, full(s));
+            tma_load_2d(sa + Geo::a_bytes, map_w, kt * kBK, n0, full(s));
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
-        const uint32_t idesc = idesc_bf16<BN>();
+        const uint32_t idesc = idesc_bf16(BN);
         bool ok = true;
         for (int kt = 0; kt < KT && ok; ++kt) {
             const int s = kt % kStages;
@@ -282,27 +307,43 @@ int vkc_gemm_bf16(const void* a, const void* w, float* c, int M, int N, int K, v
     if (!a || !w || !c) return set_error(kErrArg, "null GEMM pointer");
     if (M <= 0 || N <= 0 || K <= 0) return set_error(kErrArg, "M=%d N=%d K=%d must be positive", M, N, K);
     if (K % kBK != 0) return set_error(kErrArg, "K=%d must be a multiple of %d", K, kBK);
-    constexpr int BN = 96;
-    if (N % BN != 0) return set_error(kErrUnsupported, "N=%d must be a multiple of %d", N, BN);
+    if (N % 16 != 0) return set_error(kErrUnsupported, "N=%d must be a multiple of 16", N);
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(c)) % 16 != 0)
         return set_error(kErrArg, "A, W and C must be 16-byte aligned");
-    CUtensorMap ma, mw;
-    if (int e = make_map(&ma, a, M, K, kBM)) return e;
-    if (int e = make_map(&mw, w, N, K, BN)) return e;
+    int dev = 0, sms = 0;
+    VKC_CUDA_TRY(cudaGetDevice(&dev));
+    VKC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // Column ranges: the widest range a CTA gets is set by spreading the
+    // 16-column tiles over at most one CTA per SM; the fewest CTAs that keep
+    // that width then share the tiles in widths q*16 and (q + 1)*16 (12288
+    // columns: 128 CTAs of 96, as wide as 148 CTAs would make the widest,
+    // with less contention).  Ranges wider than kBNMax go to further waves.
+    const int tiles = N / 16;
+    const int max_tiles = kBNMax / 16 - 1;  // the wider range holds at most kBNMax columns
+    int widest = (tiles + sms - 1) / sms;
+    if (widest > max_tiles) widest = max_tiles;
+    const int ctas = (tiles + widest - 1) / widest;
+    const int q = tiles / ctas, r = tiles % ctas;
+    const int bn_lo = 16 * q;
+    const int a_rows = M <= 64 ? 64 : kBM;
+    CUtensorMap ma, mw_lo, mw_hi;
+    if (int e = make_map(&ma, a, M, K, a_rows)) return e;
+    if (int e = make_map(&mw_lo, w, N, K, bn_lo)) return e;
+    if (int e = make_map(&mw_hi, w, N, K, bn_lo + 16 <= kBNMax ? bn_lo + 16 : bn_lo)) return e;
     unsigned* status = nullptr;
     VKC_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_tc_status));
-    auto kern = gemm_tc_kernel<BN>;
-    const size_t smem = TcGeo<BN>::smem_bytes;
+    auto kern = gemm_tc_kernel;
+    const size_t smem = TcGeo::smem_bytes;
     if (int e = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(N / BN, (M + kBM - 1) / kBM, 1);
+    cfg.gridDim = dim3(ctas, (M + kBM - 1) / kBM, 1);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
     cfg.numAttrs = launch_attrs(attrs, 1);
-    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mw, c, M, N, K, status));
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mw_lo, mw_hi, c, M, N, K, r, bn_lo, a_rows, status));
     return kOk;
 }
 

@@ -508,6 +508,59 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
     }
 }
 
+// ---- Integer dot products for quantised weights ---------------------------
+// dp4a: four byte products summed into a 32-bit integer (unsigned codes times
+// signed or unsigned activation bytes).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One chunk of one column against the chunk row's 16-bit activations X (high
+// bytes xh, low bytes xl, X = 256 hi + lo): the exact integer sum of code * X
+// over the chunk, as a float.  int8: 16 codes, byte l of word w is k = 4w + l;
+// int4: 32 codes, nibble s of word w is k = 8w + s, split into the even and odd
+// nibbles as bytes (the staging holds X in that order).  |sum| < 2^27.
+template <int BITS>
+__device__ __forceinline__ float chunk_idot(const uint4 c, const uint8_t* xh, const uint8_t* xl) {
+    int hi = 0;
+    uint32_t lo = 0;
+    if constexpr (BITS == 8) {
+        const uint4 h = *reinterpret_cast<const uint4*>(xh);
+        const uint4 l = *reinterpret_cast<const uint4*>(xl);
+        hi = dp4a_us(c.x, h.x, hi);
+        hi = dp4a_us(c.y, h.y, hi);
+        hi = dp4a_us(c.z, h.z, hi);
+        hi = dp4a_us(c.w, h.w, hi);
+        lo = dp4a_uu(c.x, l.x, lo);
+        lo = dp4a_uu(c.y, l.y, lo);
+        lo = dp4a_uu(c.z, l.z, lo);
+        lo = dp4a_uu(c.w, l.w, lo);
+    } else {
+        const uint4* h4 = reinterpret_cast<const uint4*>(xh);
+        const uint4* l4 = reinterpret_cast<const uint4*>(xl);
+        const uint4 h0 = h4[0], h1 = h4[1], l0 = l4[0], l1 = l4[1];
+        const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t e = wd[w] & 0x0F0F0F0Fu, o = (wd[w] >> 4) & 0x0F0F0F0Fu;
+            hi = dp4a_us(e, hw[2 * w], hi);
+            hi = dp4a_us(o, hw[2 * w + 1], hi);
+            lo = dp4a_uu(e, lw[2 * w], lo);
+            lo = dp4a_uu(o, lw[2 * w + 1], lo);
+        }
+    }
+    return __int2float_rn(hi * 256 + static_cast<int>(lo));
+}
+
 // ---- One CTA per SM: balanced column ranges, all of K per CTA ------------
 // For matrices wide enough to give every SM at least 16 outputs.  The grid is
 // exactly one CTA per SM, so every SM streams the same number of bytes: the
@@ -528,7 +581,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const GemvPa
 // primes its ring (its weights do not depend on this kernel) and waits, so
 // consecutive launches overlap their first bytes with the previous tail.
 constexpr int kSmThreadsMax = 1024;
-constexpr int kSmHalfSmem = 112 * 1024;  // shared memory that lets two CTAs share an SM
+// Shared memory (dynamic + static) that lets two CTAs share an SM: the SM's
+// 228 KB less the 1 KB the hardware reserves per CTA, halved.
+constexpr int kSmHalfSmem = (228 - 2) * 1024 / 2;
+constexpr int kSmStaticSmem = 512;  // wred and alignment
 
 // Column range [col0, col0 + C) of CTA `cta` of `ctas` (see above); fp32 and
 // fp16 weights have no scale blocks and split N evenly in pairs.
@@ -559,16 +615,23 @@ __device__ __forceinline__ void sm_columns(int N, bool blocks, int cta, int ctas
     }
 }
 
-template <int BITS, int MODE, int kSmThreads, int D>
+template <int BITS, int MODE, int kSmThreads, int D, bool IDP>
 __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_sm_kernel(const GemvParams p) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
     constexpr int KPC = 128 / BITS;
     constexpr bool kQuant = BITS <= 8;
     constexpr bool kNorm = MODE != kGemv;
+    constexpr bool kIdp = IDP && kQuant;  // integer dot products (quantised weights)
 
     extern __shared__ __align__(16) uint8_t smem[];
-    uint4* ring = reinterpret_cast<uint4*>(smem);                                  // [NS][D][1024]
-    float* xs = reinterpret_cast<float*>(smem + NS * D * kSmThreads * 16);         // [R][NS][KPC]
+    uint4* ring = reinterpret_cast<uint4*>(smem);                                  // [NS][D][T]
+    float* xs = reinterpret_cast<float*>(smem + NS * D * kSmThreads * 16);         // [R][NS][KPC] fp32 x'
+    // integer-dot staging instead of xs: per chunk row and stream, the row's
+    // 16-bit activations as high (signed) and low (unsigned) bytes, in the
+    // order the code bytes are multiplied, and the row's scale
+    uint8_t* xh = smem + NS * D * kSmThreads * 16;                                 // [R][NS][KPC]
+    uint8_t* xl = xh + static_cast<size_t>(p.R) * NS * KPC;                        // [R][NS][KPC]
+    float* xsig = reinterpret_cast<float*>(xl + static_cast<size_t>(p.R) * NS * KPC);  // [R][NS]
     float* red = reinterpret_cast<float*>(smem);                                   // [NS][G][C], after the stream
     __shared__ float wred[kSmThreads / 32][3];
 
@@ -614,22 +677,43 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
     auto fold = [&](int base) {
 #pragma unroll
         for (int q = 0; q < kMaxAct; ++q) {
+            // Lanes hold consecutive k (base and q*T are multiples of 32), so
+            // a chunk row's KPC values sit in KPC consecutive lanes, and K (a
+            // multiple of KPC) ends on a row boundary.
             const int k = base + tid + q * kSmThreads;
-            if (k < nk) {
-                const float xv = av_x[q];
-                float xg = xv;
-                if constexpr (kNorm) {
-                    ss = fmaf(xv, xv, ss);
-                    xg = xv * av_g[q];
-                }
-                const int rl = k / KPC, i = k % KPC;
+            const bool ok = k < nk;
+            const float xv = ok ? av_x[q] : 0.f;
+            float xg = xv;
+            if constexpr (kNorm) {
+                ss = fmaf(xv, xv, ss);
+                xg = xv * av_g[q];
+            }
+            const int rl = k / KPC, i = k % KPC;
 #pragma unroll
-                for (int st = 0; st < NS; ++st) {
-                    float v = xg;
-                    if constexpr (kQuant) {
-                        v = xg * av_s[st][q];
-                        cz[st] = fmaf(xg, av_z[st][q], cz[st]);
+            for (int st = 0; st < NS; ++st) {
+                float v = xg;
+                if constexpr (kQuant) {
+                    v = xg * av_s[st][q];
+                    cz[st] = fmaf(xg, av_z[st][q], cz[st]);
+                }
+                if constexpr (kIdp) {
+                    // x' of the row as integers of 16 bits against the row's
+                    // largest magnitude m: X = rn(x' * 32767 / m), x' ~ X m / 32767
+                    float m = fabsf(v);
+#pragma unroll
+                    for (int o = KPC / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    const float inv = m > 0.f ? 32767.0f / m : 0.f;
+                    const int X = max(-32767, min(32767, __float2int_rn(v * inv)));
+                    if (ok) {
+                        // int8: byte i of the row; int4: the code word's even
+                        // nibbles (k = 8w + 0, 2, 4, 6) then its odd ones
+                        const int pos = BITS == 8 ? i : (((i >> 3) << 3) | ((i & 1) << 2) | ((i & 7) >> 1));
+                        const size_t b = static_cast<size_t>(rl * NS + st) * KPC + pos;
+                        xh[b] = static_cast<uint8_t>((X >> 8) & 0xFF);
+                        xl[b] = static_cast<uint8_t>(X & 0xFF);
+                        if (i == 0) xsig[rl * NS + st] = m * (1.0f / 32767.0f);
                     }
+                } else if (ok) {
                     if constexpr (BITS == 4) v *= int4_prescale(i);
                     xs[(rl * NS + st) * KPC + i] = v;
                 }
@@ -640,16 +724,23 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
 
     // ---- weights: prime the ring with D rows per thread -------------------
     const int my_rows = streams && grp < p.R ? (p.R - grp + G - 1) / G : 0;  // rows grp, grp+G, ...
-    auto src = [&](int st, int i) {
-        const int r = grp + i * G;
-        return reinterpret_cast<const uint4*>(p.w[st]) + (static_cast<size_t>(r) * p.N + col);
-    };
-    auto slot = [&](int st, int i) { return smem_addr(ring + (st * D + (i % D)) * kSmThreads + tid); };
+    // Row grp + i*G of column col sits at w + (grp + i*G)*N + col (16-byte
+    // units); ring slot (stream st, row i) at slot0 + (st*D + i%D)*T*16.
+    const size_t row_step = static_cast<size_t>(G) * p.N;
+    const uint4* wp[NS];
 #pragma unroll
-    for (int i = 0; i < D; ++i) {
-        if (i < my_rows)
+    for (int st = 0; st < NS; ++st)
+        wp[st] = reinterpret_cast<const uint4*>(p.w[st]) + (static_cast<size_t>(grp) * p.N + col);
+    const uint32_t slot0 = smem_addr(ring + tid);
 #pragma unroll
-            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i), src(st, i));
+    for (int u = 0; u < D; ++u) {
+        if (u < my_rows) {
+#pragma unroll
+            for (int st = 0; st < NS; ++st) {
+                cp_async16(slot0 + static_cast<uint32_t>((st * D + u) * kSmThreads * 16), wp[st]);
+                wp[st] += row_step;
+            }
+        }
         cp_async_commit();
     }
 
@@ -666,20 +757,44 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
 
     // ---- stream this thread's rows through its ring ------------------------
     uint64_t acc[NS][4];
+    float accf[NS];
 #pragma unroll
-    for (int st = 0; st < NS; ++st) acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0ull;
-    for (int i = 0; i < my_rows; ++i) {
-        cp_async_wait<D - 1>();
-        const int rl = grp + i * G;
+    for (int st = 0; st < NS; ++st) {
+        acc[st][0] = acc[st][1] = acc[st][2] = acc[st][3] = 0ull;
+        accf[st] = 0.f;
+    }
+    // Unrolled by the ring depth, so every slot offset is a constant; the
+    // weight and activation pointers advance by whole rows.
+    const float* xrow = xs + grp * NS * KPC;
+    const int xstep = G * NS * KPC;
+    int xr = grp;  // chunk row (integer-dot staging)
+    for (int i = 0; i < my_rows; i += D) {
 #pragma unroll
-        for (int st = 0; st < NS; ++st) {
-            const uint4 chunk = ring[(st * D + (i % D)) * kSmThreads + tid];
-            chunk_fma<BITS>(chunk, xs + (rl * NS + st) * KPC, acc[st]);
+        for (int u = 0; u < D; ++u) {
+            if (i + u < my_rows) {
+                cp_async_wait<D - 1>();
+#pragma unroll
+                for (int st = 0; st < NS; ++st) {
+                    const uint4 chunk = ring[(st * D + u) * kSmThreads + tid];
+                    if constexpr (kIdp) {
+                        const int off = (xr * NS + st) * KPC;
+                        accf[st] = fmaf(xsig[xr * NS + st], chunk_idot<BITS>(chunk, xh + off, xl + off), accf[st]);
+                    } else {
+                        chunk_fma<BITS>(chunk, xrow + st * KPC, acc[st]);
+                    }
+                }
+                xrow += xstep;
+                xr += G;
+                if (i + u + D < my_rows) {
+#pragma unroll
+                    for (int st = 0; st < NS; ++st) {
+                        cp_async16(slot0 + static_cast<uint32_t>((st * D + u) * kSmThreads * 16), wp[st]);
+                        wp[st] += row_step;
+                    }
+                }
+                cp_async_commit();
+            }
         }
-        if (i + D < my_rows)
-#pragma unroll
-            for (int st = 0; st < NS; ++st) cp_async16(slot(st, i + D), src(st, i + D));
-        cp_async_commit();
     }
     cp_async_wait<0>();
 
@@ -696,9 +811,13 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
     if (streams) {
 #pragma unroll
         for (int st = 0; st < NS; ++st) {
-            const float2 a = f2_unpack(acc[st][0]), b = f2_unpack(acc[st][1]);
-            const float2 c2 = f2_unpack(acc[st][2]), d = f2_unpack(acc[st][3]);
-            red[(st * G + grp) * C + c] = ((a.x + a.y) + (b.x + b.y)) + ((c2.x + c2.y) + (d.x + d.y));
+            if constexpr (kIdp) {
+                red[(st * G + grp) * C + c] = accf[st];
+            } else {
+                const float2 a = f2_unpack(acc[st][0]), b = f2_unpack(acc[st][1]);
+                const float2 c2 = f2_unpack(acc[st][2]), d = f2_unpack(acc[st][3]);
+                red[(st * G + grp) * C + c] = ((a.x + a.y) + (b.x + b.y)) + ((c2.x + c2.y) + (d.x + d.y));
+            }
         }
     }
     __syncthreads();
@@ -1258,10 +1377,12 @@ int sm_count(int* out) {
     return kOk;
 }
 
-// Which single-vector GEMV kernel runs (vkc_set_gemv_plan): 0 chooses per
-// shape, 1 always the cluster split-K kernel, 2 the one-CTA-per-SM kernel in
-// its full-SM shape wherever it can run, 3 the same in its half-SM shape.
-int g_gemv_plan = 0;
+// Which single-vector GEMV kernel runs (vkc_set_gemv_plan), per host thread:
+// 0 chooses per shape (half-SM shape for the per-SM kernel), 1 always the
+// cluster split-K kernel, 2 the one-CTA-per-SM kernel in its full-SM shape
+// wherever it can run, 3 the same in its half-SM shape, 4 chooses per shape
+// with the full-SM shape.
+thread_local int g_gemv_plan = 0;
 
 constexpr size_t kSmMaxDynamicSmem = 220 * 1024;
 
@@ -1286,7 +1407,7 @@ SmShape sm_shape(int NS, int K, bool half) {
         for (int d : depths) {
             if (NS == 2 && d > 4) continue;  // 64 KB ring for two streams
             const size_t b = sm_smem_bytes(NS, 512, d, K);
-            if (b + 1024 <= static_cast<size_t>(kSmHalfSmem)) {
+            if (b + kSmStaticSmem <= static_cast<size_t>(kSmHalfSmem)) {
                 sh.T = 512;
                 sh.D = d;
                 sh.smem = b;
@@ -1310,14 +1431,27 @@ bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh) {
     // every CTA gets at least one pair of outputs, and at most T - 2 outputs
     if (BITS <= 8 && (p.N / kGroup > sms || (sms + p.N / kGroup - 1) / (p.N / kGroup) > kGroup / 2)) return false;
     if (BITS > 8 && (p.N / 2 < sms || p.N / sms > sh.T - 2)) return false;
-    if (g_gemv_plan >= 2) return true;
+    if (g_gemv_plan == 2 || g_gemv_plan == 3) return true;
     return p.N >= 16 * sms;
 }
 
-template <int BITS, int MODE, int T, int D>
-int launch_sm_shape(const GemvParams& p, cudaStream_t stream, int sms, size_t smem) {
-    const void* kern = reinterpret_cast<const void*>(gemv_sm_kernel<BITS, MODE, T, D>);
+// Quantised weights on the per-SM kernel use integer dot products
+// (vkc_set_gemv_int_dot), per host thread.
+thread_local bool g_gemv_idp = true;
+
+template <int BITS, int MODE, int T, int D, bool IDP>
+int launch_sm_shape_k(const GemvParams& p, cudaStream_t stream, int sms, size_t smem) {
+    const void* kern = reinterpret_cast<const void*>(gemv_sm_kernel<BITS, MODE, T, D, IDP>);
     if (int e = ensure_smem(kern, smem)) return e;
+    if (T == 512) {
+        // the largest shared-memory carveout, so that two CTAs fit on an SM
+        static bool carveout_set = false;
+        if (!carveout_set) {
+            VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                              cudaSharedmemCarveoutMaxShared));
+            carveout_set = true;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms, 1, 1);
     cfg.blockDim = dim3(T, 1, 1);
@@ -1326,8 +1460,16 @@ int launch_sm_shape(const GemvParams& p, cudaStream_t stream, int sms, size_t sm
     cudaLaunchAttribute attrs[2];
     cfg.attrs = attrs;
     cfg.numAttrs = launch_attrs(attrs, 1);
-    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_sm_kernel<BITS, MODE, T, D>, p));
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_sm_kernel<BITS, MODE, T, D, IDP>, p));
     return kOk;
+}
+
+template <int BITS, int MODE, int T, int D>
+int launch_sm_shape(const GemvParams& p, cudaStream_t stream, int sms, size_t smem) {
+    if constexpr (BITS <= 8) {
+        if (g_gemv_idp) return launch_sm_shape_k<BITS, MODE, T, D, true>(p, stream, sms, smem);
+    }
+    return launch_sm_shape_k<BITS, MODE, T, D, false>(p, stream, sms, smem);
 }
 
 template <int BITS, int MODE>
@@ -1352,7 +1494,7 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
     if (g_gemv_plan != 1) {
-        const SmShape sh = sm_shape(NS, p.K, g_gemv_plan != 2);
+        const SmShape sh = sm_shape(NS, p.K, g_gemv_plan == 0 || g_gemv_plan == 3);
         if (sm_kernel_fits<BITS, MODE>(p, sms, sh)) return launch_sm<BITS, MODE>(p, stream, sms, sh);
     }
     // Widest tile and smallest cluster that put at least two CTAs on every SM.
@@ -1874,11 +2016,14 @@ int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const 
 // Status word of the current device (bits: kStatus*).  Reading waits for the
 // device; `clear` resets it.
 int vkc_set_gemv_plan(int plan) {
-    if (plan < 0 || plan > 3) return set_error(kErrArg, "GEMV plan %d (expected 0 to 3)", plan);
+    if (plan < 0 || plan > 4) return set_error(kErrArg, "GEMV plan %d (expected 0 to 4)", plan);
     g_gemv_plan = plan;
     return kOk;
 }
 int vkc_get_gemv_plan(void) { return g_gemv_plan; }
+
+void vkc_set_gemv_int_dot(int enable) { g_gemv_idp = enable != 0; }
+int vkc_get_gemv_int_dot(void) { return g_gemv_idp ? 1 : 0; }
 
 void vkc_wait_limits(uint64_t* peer_ns, uint64_t* cluster_ns) {
     if (peer_ns) *peer_ns = kPeerWaitNs;

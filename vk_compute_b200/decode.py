@@ -167,12 +167,65 @@ def build_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: i
     g = torch.Generator(device=device).manual_seed(base + 6)
     g_attn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
     g_ffn = 1 + 0.1 * torch.randn(H, generator=g, device=device)
+    kcache, vcache = _cache_shard(cfg, plan, layer, device, seed, g)
+    return LayerShard(qkv, o, gate, up, down, g_attn, g_ffn, kcache, vcache)
+
+
+def _cache_shard(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, seed: int, g=None):
+    """The KV-cache contents of earlier tokens, N(0, 1), this rank's heads
+    (drawn after the two norm vectors of build_layer's generator)."""
+    H = cfg.hidden
+    if g is None:
+        g = torch.Generator(device=device).manual_seed(seed * 1000 + layer * 10 + 6)
+        torch.randn(H, generator=g, device=device)
+        torch.randn(H, generator=g, device=device)
     # Cache contents of earlier tokens: N(0, 1), the rank's KV heads.
     kfull = torch.randn(cfg.ctx, cfg.n_kv, cfg.head_dim, generator=g, device=device).half()
     vfull = torch.randn(cfg.n_kv, cfg.head_dim // 8, cfg.ctx, 8, generator=g, device=device).half()
     k0, k1 = plan.kv_heads
     kcache = kfull[:, k0:k1].contiguous()
     vcache = vfull[k0:k1].contiguous()
+    return kcache, vcache
+
+
+LAYER_MATRICES = ("qkv", "o", "gate", "up", "down")
+
+
+def save_model(layers: list[LayerShard], path: str) -> None:
+    """Writes the layers of an unsharded (one-GPU) model to a weights file
+    (ops.save_weights): per layer the five packed matrices and the two norm
+    vectors, a vector of K values being a K x 1 fp32 matrix, whose chunk
+    layout is the plain vector."""
+    weights = {}
+    for i, L in enumerate(layers):
+        for m in LAYER_MATRICES:
+            weights[f"layers.{i}.{m}"] = getattr(L, m)
+        for g in ("g_attn", "g_ffn"):
+            v = getattr(L, g)
+            weights[f"layers.{i}.{g}"] = ops.PackedWeight(32, v.numel(), 1, v.view(torch.uint8), None, None)
+    ops.save_weights(path, weights)
+
+
+def load_layer(cfg: DecoderConfig, plan: ShardPlan, layer: int, device, full: dict, seed: int = 0) -> LayerShard:
+    """This rank's shard of layer `layer` cut from the unsharded matrices in
+    `full` (ops.load_weights of a save_model file): QKV by its two output
+    ranges, gate/up by output rows, O and down by input rows -- the same
+    shards build_layer draws.  The KV caches of earlier tokens are drawn as
+    build_layer draws them."""
+    pre = f"layers.{layer}."
+    hd = cfg.head_dim
+    q_lo, q_hi = plan.q_heads[0] * hd, plan.q_heads[1] * hd
+    kv_lo = cfg.n_q * hd + 2 * plan.kv_heads[0] * hd
+    kv_hi = cfg.n_q * hd + 2 * plan.kv_heads[1] * hd
+    f_lo, f_hi = plan.ffn_rows
+    qkv = full[pre + "qkv"].columns([(q_lo, q_hi), (kv_lo, kv_hi)])
+    o = full[pre + "o"].rows(*plan.o_k)
+    gate = full[pre + "gate"].shard(f_lo, f_hi)
+    up = full[pre + "up"].shard(f_lo, f_hi)
+    down = full[pre + "down"].rows(f_lo, f_hi)
+    g_attn = full[pre + "g_attn"].packed.view(torch.float32).clone()
+    g_ffn = full[pre + "g_ffn"].packed.view(torch.float32).clone()
+    kcache, vcache = _cache_shard(cfg, plan, layer, device, seed)
     return LayerShard(qkv, o, gate, up, down, g_attn, g_ffn, kcache, vcache)
 
 
@@ -261,7 +314,21 @@ class ShardedDecoder:
             self.peer.close()
             self.peer = None
 
+    # The GEMVs of a step run one 1024-thread CTA per SM (or clusters, for
+    # small shards): a 512-thread GEMV CTA resident beside the attention
+    # kernel would leave room for only one of its two CTAs per SM and split
+    # its clustered grid into two waves.
+    GEMV_PLAN = "auto-full"
+
     def step(self, pos: int) -> torch.Tensor:
+        prev = ops.get_gemv_plan()
+        ops.set_gemv_plan(self.GEMV_PLAN)
+        try:
+            return self._step(pos)
+        finally:
+            ops.set_gemv_plan(prev)
+
+    def _step(self, pos: int) -> torch.Tensor:
         cfg, p, b = self.cfg, self.plan, self.buf
         if not 0 <= pos < cfg.ctx:
             raise ValueError(f"position {pos} outside the cache of {cfg.ctx} tokens")

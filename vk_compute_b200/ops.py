@@ -63,6 +63,81 @@ class PackedWeight:
             z = self.zero.view(self.N // GROUP, self.K)[lo // GROUP:hi // GROUP].contiguous().view(-1)
         return PackedWeight(self.bits, self.K, hi - lo, p, s, z)
 
+    def columns(self, ranges: list[tuple[int, int]]) -> "PackedWeight":
+        """Copy of the outputs in `ranges` ([lo, hi) pairs, concatenated in
+        order): a row shard of W^T made of several row ranges."""
+        parts = [self.shard(lo, hi) for lo, hi in ranges]
+        if len(parts) == 1:
+            return parts[0]
+        R = self.K // chunk_elems(self.bits)
+        n = sum(p.N for p in parts)
+        p = torch.cat([q.packed.view(R, q.N, 16) for q in parts], dim=1).contiguous().view(-1)
+        s = z = None
+        if self.scale is not None:
+            s = torch.cat([q.scale.view(q.N // GROUP, self.K) for q in parts]).contiguous().view(-1)
+            z = torch.cat([q.zero.view(q.N // GROUP, self.K) for q in parts]).contiguous().view(-1)
+        return PackedWeight(self.bits, self.K, n, p, s, z)
+
+    def rows(self, lo: int, hi: int) -> "PackedWeight":
+        """Copy of inputs [lo, hi) (a K-split shard: y_partial = W[lo:hi]^T
+        x[lo:hi]).  Chunk rows are whole runs of 128/bits inputs, so the
+        shard is a contiguous byte range; scale/zero keep their blocks."""
+        kpc = chunk_elems(self.bits)
+        if lo % kpc or hi % kpc:
+            raise ValueError(f"a {self.bits}-bit K-split shard must start and end on {kpc}-input chunks")
+        R = self.K // kpc
+        p = self.packed.view(R, self.N, 16)[lo // kpc:hi // kpc].contiguous().view(-1)
+        s = z = None
+        if self.scale is not None:
+            s = self.scale.view(self.N // GROUP, self.K)[:, lo:hi].contiguous().view(-1)
+            z = self.zero.view(self.N // GROUP, self.K)[:, lo:hi].contiguous().view(-1)
+        return PackedWeight(self.bits, hi - lo, self.N, p, s, z)
+
+
+def save_weights(path: str, weights: dict[str, PackedWeight]) -> None:
+    """Writes named packed matrices to `path` in the device layout
+    (vkc_weights_write; the arrays are copied to host memory first)."""
+    from ._lib import WeightEntry
+
+    entries = (WeightEntry * len(weights))()
+    keep = []
+    for e, (name, w) in zip(entries, weights.items()):
+        if len(name.encode()) >= 64:
+            raise ValueError(f"matrix name {name!r} is longer than 63 bytes")
+        e.name, e.bits, e.K, e.N = name.encode(), w.bits, w.K, w.N
+        arrs = [w.packed.cpu().contiguous()]
+        if w.scale is not None:
+            arrs += [w.scale.cpu().contiguous(), w.zero.cpu().contiguous()]
+        keep.append(arrs)
+        e.data = arrs[0].data_ptr()
+        if w.scale is not None:
+            e.scale, e.zero = arrs[1].data_ptr(), arrs[2].data_ptr()
+    check(lib().vkc_weights_write(str(path).encode(), entries, len(weights)))
+
+
+def load_weights(path: str, device="cuda", names=None, stream=None) -> dict[str, PackedWeight]:
+    """Reads named matrices (all, or `names`) from a vkc_weights_write file
+    straight into device memory."""
+    from ._lib import WeightEntry
+
+    f = C.c_void_p()
+    check(lib().vkc_weights_open(str(path).encode(), C.byref(f)))
+    out = {}
+    try:
+        n = lib().vkc_weights_count(f)
+        for i in range(n):
+            info = WeightEntry()
+            check(lib().vkc_weights_info(f, i, C.byref(info)))
+            name = info.name.decode()
+            if names is not None and name not in names:
+                continue
+            w = _alloc_weight(info.bits, info.K, info.N, device)
+            check(lib().vkc_weights_read(f, i, _p(w.packed), _p(w.scale), _p(w.zero), _s(stream)))
+            out[name] = w
+    finally:
+        lib().vkc_weights_close(f)
+    return out
+
 
 def _alloc_weight(bits: int, K: int, N: int, device) -> PackedWeight:
     packed = torch.empty(K * N * bits // 8, dtype=torch.uint8, device=device)
@@ -318,7 +393,7 @@ def get_pdl() -> bool:
     return bool(lib().vkc_get_pdl())
 
 
-GEMV_PLANS = {"auto": 0, "cluster": 1, "per-sm": 2, "per-sm-half": 3}
+GEMV_PLANS = {"auto": 0, "cluster": 1, "per-sm": 2, "per-sm-half": 3, "auto-full": 4}
 
 
 def set_gemv_plan(plan: str) -> None:
@@ -326,8 +401,35 @@ def set_gemv_plan(plan: str) -> None:
     chooses per shape, "cluster" always splits K across a cluster, "per-sm"
     runs one CTA per SM with whole-K column ranges wherever it can (a 1024-
     thread CTA owning the SM), "per-sm-half" the same with a 512-thread CTA
-    that leaves half the SM to the next launch."""
+    that leaves half the SM to the next launch, "auto-full" chooses per shape
+    with the 1024-thread CTA.  Per host thread."""
     check(lib().vkc_set_gemv_plan(GEMV_PLANS[plan]))
+
+
+def set_gemv_int_dot(enable: bool) -> None:
+    """8/4-bit weights on the per-SM GEMV kernel: integer dot products over
+    16-bit activations per chunk row (True, the default) or fp32 FMAs
+    (vkc_set_gemv_int_dot).  Per host thread."""
+    lib().vkc_set_gemv_int_dot(int(enable))
+
+
+def get_gemv_int_dot() -> bool:
+    return bool(lib().vkc_get_gemv_int_dot())
+
+
+ATTENTION_PLANS = {"auto": 0, "clustered": 1, "per-sm": 2}
+
+
+def set_attention_plan(plan: str) -> None:
+    """Decode attention's split of the cache (vkc_set_attention_plan):
+    "auto" per shape, "clustered" (clusters of 8 CTAs per KV head, two CTAs
+    per SM), "per-sm" (at most one CTA per SM, deep ring).  Per host thread."""
+    check(lib().vkc_set_attention_plan(ATTENTION_PLANS[plan]))
+
+
+def get_attention_plan() -> str:
+    v = lib().vkc_get_attention_plan()
+    return next(k for k, n in ATTENTION_PLANS.items() if n == v)
 
 
 def get_gemv_plan() -> str:
