@@ -54,10 +54,11 @@ void vkc_set_timing(int enable);
 int vkc_get_timing(void);
 /* Which kernel runs the single-vector GEMV family (vkc_gemv,
  * vkc_rmsnorm_gemv, -rope, -rope_kv, -swiglu, vkc_gemv_residual / _peer):
- * 0 (default) chooses per shape -- one 1024-thread CTA per SM, each with a
- * balanced range of whole-K output columns, when every SM gets at least 16
- * outputs and the input is not a peer exchange; otherwise clusters that split
- * K and reduce in distributed shared memory.  1 always uses the cluster
+ * 0 (default) chooses per shape -- one CTA per SM (512 threads for
+ * single-stream fp16/fp32 weights, 1024 otherwise), each with a balanced range
+ * of whole-K output columns, when every SM gets at least 16 outputs and the
+ * input is not a peer exchange; otherwise clusters that split K and reduce in
+ * distributed shared memory.  1 always uses the cluster
  * kernel; 2 uses the one-CTA-per-SM kernel with 1024-thread CTAs wherever it
  * can run, 3 with 512-thread CTAs that leave half of each SM to the next
  * launch, 4 chooses per shape like 0 but with 1024-thread CTAs (for chains

@@ -1378,10 +1378,11 @@ int sm_count(int* out) {
 }
 
 // Which single-vector GEMV kernel runs (vkc_set_gemv_plan), per host thread:
-// 0 chooses per shape (half-SM shape for the per-SM kernel), 1 always the
-// cluster split-K kernel, 2 the one-CTA-per-SM kernel in its full-SM shape
-// wherever it can run, 3 the same in its half-SM shape, 4 chooses per shape
-// with the full-SM shape.
+// 0 chooses per shape (the per-SM kernel's half-SM shape for single-stream
+// fp16/fp32 weights, its full-SM shape otherwise), 1 always the cluster
+// split-K kernel, 2 the one-CTA-per-SM kernel in its full-SM shape wherever it
+// can run, 3 the same in its half-SM shape, 4 chooses per shape with the
+// full-SM shape.
 thread_local int g_gemv_plan = 0;
 
 constexpr size_t kSmMaxDynamicSmem = 220 * 1024;
@@ -1494,7 +1495,11 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
     if (g_gemv_plan != 1) {
-        const SmShape sh = sm_shape(NS, p.K, g_gemv_plan == 0 || g_gemv_plan == 3);
+        // automatic shape: 512 threads for single-stream fp16/fp32 weights
+        // (their FMA loop gains from the next launch's early ring), 1024
+        // threads for 8/4-bit weights and two streams (more bytes in flight)
+        const bool half = g_gemv_plan == 3 || (g_gemv_plan == 0 && BITS >= 16 && NS == 1);
+        const SmShape sh = sm_shape(NS, p.K, half);
         if (sm_kernel_fits<BITS, MODE>(p, sms, sh)) return launch_sm<BITS, MODE>(p, stream, sms, sh);
     }
     // Widest tile and smallest cluster that put at least two CTAs on every SM.
