@@ -153,3 +153,40 @@ def test_timing_switch(sess):
     assert_close(D.read_buffer(sess, y), ref, TOL[8], "GEMV-INT8, timing on")
     for b in (xb, wb, sb, zb, y):
         D.destroy_buffer(sess, b)
+
+
+@pytest.mark.parametrize("nbytes", [4, 17, 16384, 49157, 1 << 20, (1 << 20) + 12])
+def test_write_buffer_round_trip(sess, nbytes):
+    """writeBuffer (an extension of the ABI) into an existing buffer: staged
+    sizes up to 1 MiB, ragged tails and the larger synchronous path."""
+    rng = np.random.default_rng(nbytes)
+    a = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    b = D.create_buffer(sess, None, nbytes)
+    D.write_buffer(sess, b, a)
+    np.testing.assert_array_equal(D.read_buffer(sess, b, np.uint8), a)
+    D.destroy_buffer(sess, b)
+
+
+def test_write_buffer_sequence_then_operator(sess):
+    """Several uploads without a read in between (both staging slots reused,
+    the caller's array overwritten at once), then an operator on the last
+    value written: the operator sees it, the other buffers keep theirs."""
+    x_last = host_vector(SEED_X + 5, K)
+    xs = [host_vector(SEED_X + i, K) for i in range(5)] + [x_last]
+    xb = D.create_buffer(sess, None, 4 * K)
+    side = [D.create_buffer(sess, None, 4 * K) for _ in range(3)]
+    scratch = np.empty(K, dtype=np.float32)
+    for i, x in enumerate(xs):
+        scratch[:] = x
+        D.write_buffer(sess, xb, scratch)
+        D.write_buffer(sess, side[i % 3], scratch)
+        scratch[:] = -1.0  # reused by the caller as soon as the call returns
+    w, sc, zr, host = packed(SEED_W, 8)
+    y = D.create_buffer(sess, None, 4 * N)
+    wb, sb, zb = bufs(sess, w, sc, zr)
+    D.execute(sess, [D.operation("GEMV-INT8.spv", [xb, wb, y, sb, zb], [1, N, K])])
+    assert_close(D.read_buffer(sess, y), o.qgemv(x_last, None, *host, 8, K, N), TOL[8], "GEMV-INT8 after writes")
+    for i in range(3):
+        np.testing.assert_array_equal(D.read_buffer(sess, side[i]), xs[3 + i])
+    for b in [xb, y, wb, sb, zb] + side:
+        D.destroy_buffer(sess, b)

@@ -49,16 +49,24 @@ def test_rmsnorm_gemv_batched(bits, K, N, M):
         assert_close(y[m], ref, TOL[bits], f"batched RmsNorm-GEMV bits={bits} K={K} N={N} m={m}/{M}")
 
 
-def test_batched_rows_match_single_vector_kernel():
-    """Row m of a batch equals the one-vector kernel on x[m] to fp32 rounding."""
+@pytest.mark.parametrize("int_dot,bar", [(False, 1e-5), (True, 1e-4)])
+def test_batched_rows_match_single_vector_kernel(int_dot, bar):
+    """Row m of a batch equals the one-vector kernel on x[m]: to fp32
+    rounding against its fp32 arithmetic, and to the 16-bit activation steps
+    (about 1e-5 relative) against its integer dot products."""
     K, N = 4096, 12288
     w = device_weight(SEED_W, K, N, 8)
     x = torch.stack([device_vector(7000 + m, K) for m in range(6)])
     y = ops.gemv_batched(w, x)
-    for m in range(6):
-        single = ops.gemv(w, x[m].contiguous())
-        err = (y[m] - single).abs().max().item() / single.abs().max().item()
-        assert err < 1e-5, (m, err)
+    before = ops.get_gemv_int_dot()
+    ops.set_gemv_int_dot(int_dot)
+    try:
+        for m in range(6):
+            single = ops.gemv(w, x[m].contiguous())
+            err = (y[m] - single).abs().max().item() / single.abs().max().item()
+            assert err < bar, (m, err)
+    finally:
+        ops.set_gemv_int_dot(before)
 
 
 def test_batched_rejects_bad_m():

@@ -126,9 +126,11 @@ struct Ctx {
     cudaStream_t stream;
     cudaEvent_t ev_begin, ev_end;
     bool timed;
-    // Pinned staging for small writeBuffer uploads: the caller's bytes are
-    // copied here, so the call can return before the device copy has run.
+    // Mapped pinned staging for small writeBuffer uploads: the caller's
+    // bytes are copied here, so the call can return before the device copy
+    // has run; a kernel reads them through stage_dev.
     void* stage[2];
+    void* stage_dev[2];
     bool stage_busy[2];  // an upload from the slot may still be in flight
     int next;
     void* rstage;  // mapped pinned landing buffer for small reads
@@ -138,19 +140,23 @@ constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronous
 
 void stream_synced(Ctx* c) { c->stage_busy[0] = c->stage_busy[1] = false; }
 
-// Device -> mapped host copy for readBuffer: a kernel rather than a DMA copy
-// (lower latency for the kilobytes a decode step reads back).  It may be
-// launched while the previous kernel still runs (programmatic dependent
-// launch) and reads only after that kernel's writes are visible.
-__global__ void download_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
-                                uint8_t* __restrict__ dst_tail, const uint8_t* __restrict__ src_tail, int tail) {
+// Copies between device memory and mapped pinned host memory for the small
+// buffers of readBuffer and writeBuffer: a kernel rather than a DMA copy
+// (lower latency for the kilobytes a decode step moves, and no host time
+// spent feeding the copy engine).  It may be launched while the previous
+// kernel still runs (programmatic dependent launch): it lets the next kernel
+// start its own prologue at once, and touches memory only after the previous
+// kernel's writes are visible and its reads are done.
+__global__ void copy16_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
+                              uint8_t* __restrict__ dst_tail, const uint8_t* __restrict__ src_tail, int tail) {
+    pdl_launch_dependents();
     pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
     if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < tail) dst_tail[threadIdx.x] = src_tail[threadIdx.x];
 }
 
-cudaError_t launch_download(void* dst, const void* src, size_t n, cudaStream_t stream) {
+cudaError_t launch_copy16(void* dst, const void* src, size_t n, cudaStream_t stream) {
     const size_t n16 = n / 16;
     const int tail = static_cast<int>(n % 16);
     int blocks = static_cast<int>((n16 + 255) / 256);
@@ -165,7 +171,7 @@ cudaError_t launch_download(void* dst, const void* src, size_t n, cudaStream_t s
     attr.val.programmaticStreamSerializationAllowed = 1;  // safe whatever vkc_set_pdl says: it waits first
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, download_kernel, static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
+    return cudaLaunchKernelEx(&cfg, copy16_kernel, static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
                               static_cast<uint8_t*>(dst) + n16 * 16, static_cast<const uint8_t*>(src) + n16 * 16,
                               tail);
 }
@@ -478,6 +484,7 @@ device createDevice() {
     check_cuda(cudaEventCreate(&c->ev_end), "cudaEventCreate");
     for (int i = 0; i < 2; ++i) {
         c->stage[i] = nullptr;
+        c->stage_dev[i] = nullptr;
         c->stage_busy[i] = false;
     }
     c->next = 0;
@@ -563,7 +570,7 @@ void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* outpu
             check_cuda(cudaHostAlloc(&c->rstage, kStageMax, cudaHostAllocMapped), "cudaHostAlloc");
             check_cuda(cudaHostGetDevicePointer(&c->rstage_dev, c->rstage, 0), "cudaHostGetDevicePointer");
         }
-        check_cuda(launch_download(c->rstage_dev, buf.buffer, n, c->stream), "download kernel");
+        check_cuda(launch_copy16(c->rstage_dev, buf.buffer, n, c->stream), "read-back kernel");
         check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
         stream_synced(c);
         memcpy(output, c->rstage, n);
@@ -575,10 +582,12 @@ void readBuffer(VkDevice dev, VkPhysicalDevice, VkQueue, buffer buf, void* outpu
     stream_synced(c);
 }
 
-// Uploads of up to kStageMax bytes go through the pinned staging buffer and
-// return once the bytes are staged (the caller may reuse `data` at once); the
-// device copy is ordered before every later operation on the session stream.
-// Larger uploads are copied synchronously.
+// Uploads of up to kStageMax bytes go through a mapped pinned staging buffer
+// and return once the bytes are staged (the caller may reuse `data` at once);
+// the device copy, a kernel reading the staging buffer over the bus, is
+// ordered before every later operation on the session stream.  (A DMA copy
+// of a few kilobytes costs several microseconds of host time in the driver;
+// the kernel launch about two.)  Larger uploads are copied synchronously.
 void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
     Ctx* c = ctx_of(dev);
     if (!buf.buffer) fatal("writeBuffer: empty buffer");
@@ -599,9 +608,12 @@ void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
         check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
         stream_synced(c);
     }
-    if (!c->stage[slot]) check_cuda(cudaHostAlloc(&c->stage[slot], kStageMax, cudaHostAllocDefault), "cudaHostAlloc");
+    if (!c->stage[slot]) {
+        check_cuda(cudaHostAlloc(&c->stage[slot], kStageMax, cudaHostAllocMapped), "cudaHostAlloc");
+        check_cuda(cudaHostGetDevicePointer(&c->stage_dev[slot], c->stage[slot], 0), "cudaHostGetDevicePointer");
+    }
     memcpy(c->stage[slot], data, n);
-    check_cuda(cudaMemcpyAsync(buf.buffer, c->stage[slot], n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
+    check_cuda(launch_copy16(buf.buffer, c->stage_dev[slot], n, c->stream), "upload kernel");
     c->stage_busy[slot] = true;
 }
 
