@@ -540,13 +540,15 @@ def decode_parity(dec, cfg, rank: int, world: int, device, pos: int) -> dict | N
                        "from the same x at the same position"}
 
 
-def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float, parity: bool = True):
+def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float, parity: bool = True,
+                      shape: str = "full"):
     """The 36-layer decoder chain (hidden 4096, 32 query / 8 KV heads of 128,
     intermediate 12288, int4 weights ~N(0,0.02), random-init) for one token at
     position 8191 (attention over a full 8192-token fp16 cache), sharded over
     `world` GPUs by heads (QKV, attention), input rows (O, down) and output
     rows (gate/up) with two all-reduces per layer (the library's NVLink peer
-    all-reduce).  Steps are graph launches; time is the max over ranks."""
+    all-reduce).  `shape` is the decoder's kernel shape (ShardedDecoder).
+    Steps are graph launches; time is the max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -554,7 +556,7 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
 
     cfg = DecoderConfig()
     t0 = time.perf_counter()
-    dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7)
+    dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7, shape=shape)
     pos = cfg.ctx - 1
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
@@ -595,7 +597,7 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
     kernels = dec.kernels_per_step()
     exchange = dec.exchange
     dec.close()
-    return {"layers": cfg.layers, "us_per_step": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
+    return {"layers": cfg.layers, "shape": shape, "us_per_step": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
             "bytes_per_step": rank_bytes * world, "GB_s": round(rank_bytes * world / us / 1e3, 1),
             "frac_of_peak_per_gpu": round(rank_bytes / us / 1e3 / peak, 4),
             "kernels_per_step": kernels, "all_reduces_per_step": 2 * cfg.layers if world > 1 else 0,
@@ -766,6 +768,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config measurements beside the headline (N=1)")
     ap.add_argument("--decode-steps", type=int, default=20)
+    ap.add_argument("--decode-shape", default="full", choices=["full", "half"],
+                    help="kernel shapes of the decode step (see ShardedDecoder)")
     ap.add_argument("--clock-window", type=float, default=1.5, help="seconds of sampled load before timing")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -921,7 +925,7 @@ def main():
     if not args.no_decode:
         torch.cuda.synchronize()
         decode = decode_step_bench(rank, world, device, max(1, args.decode_steps), 3, peak,
-                                   parity=not args.no_decode_parity)
+                                   parity=not args.no_decode_parity, shape=args.decode_shape)
 
     configs = None
     if world == 1 and args.workload == "rmsnorm_gemv_int8" and not args.no_configs:

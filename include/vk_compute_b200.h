@@ -219,7 +219,10 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
  * host thread: 0 (default) chooses per shape; 1 clusters of 8 CTAs per KV
  * head merging in distributed shared memory, two CTAs per SM; 2 at most one
  * CTA per SM, each streaming a long token range through a deep ring, the
- * splits of a head merged by the last to finish.  The workspace size
+ * splits of a head merged by the last to finish; 3 the same with a 3-stage
+ * ring in at most half an SM's shared memory (so the next kernel in the
+ * stream can be resident beside it under programmatic dependent launch).
+ * The workspace size
  * (vkc_attention_workspace_bytes) depends on the plan in force.  No
  * counterpart in the reference. */
 int vkc_set_attention_plan(int plan);

@@ -40,9 +40,10 @@ def ref_attention(q, kc, vc, n_q, n_kv, hd, ctx, scale):
     return out
 
 
-def test_decoder_two_layers_two_tokens():
+@pytest.mark.parametrize("shape", ["full", "half"])
+def test_decoder_two_layers_two_tokens(shape):
     cfg = CFG
-    dec = ShardedDecoder(cfg, seed=3)
+    dec = ShardedDecoder(cfg, seed=3, shape=shape)
     H, I, hd = cfg.hidden, cfg.inter, cfg.head_dim
     # host copies of every layer (same dense matrices, oracle quantiser)
     host = []

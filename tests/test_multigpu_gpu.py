@@ -40,13 +40,23 @@ def _init(rank, world, port):
 
 
 def _gather_child(rank, world, port, out_dir):
+    """The exchanges have no "buffer free" handshake (a consumer kernel
+    finishes reading before its own next exchange arrives), so a host-side
+    check of a rank's buffer is followed by a barrier before any rank starts
+    the next round and writes into it again.  Failed checks are recorded by
+    name."""
     dist = _init(rank, world, port)
+    bad = []
+
+    def check(label, cond):
+        if not cond:
+            bad.append(label)
+
     from vk_compute_b200.p2p import PeerGather
 
     dev = torch.device("cuda", rank)
     n = 1024
     pg = PeerGather({"v": n * world, "w": 3 * 256 * world, "r": 2048 * world}, dev)
-    ok = True
     part = torch.empty(n, device=dev)
     part2 = torch.empty(3 * 256, device=dev)
     # eager rounds
@@ -57,9 +67,10 @@ def _gather_child(rank, world, port, out_dir):
         pg.gather("w", part2)
         torch.cuda.synchronize(dev)
         want = torch.cat([torch.arange(n, dtype=torch.float32) + 1000 * r + 7 * it for r in range(world)])
-        ok &= bool(torch.equal(pg.buffers["v"].cpu(), want))
+        check(f"eager v {it}", torch.equal(pg.buffers["v"].cpu(), want))
         want2 = torch.cat([torch.full((3 * 256,), float(r * 10 + it)) for r in range(world)])
-        ok &= bool(torch.equal(pg.buffers["w"].cpu(), want2))
+        check(f"eager w {it}", torch.equal(pg.buffers["w"].cpu(), want2))
+        dist.barrier()
     # graph replays: the counters keep growing, nothing is reset
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
@@ -77,9 +88,10 @@ def _gather_child(rank, world, port, out_dir):
         g.replay()
         torch.cuda.synchronize(dev)
         want = torch.cat([torch.full((n,), float(100 * r + it)) for r in range(world)])
-        ok &= bool(torch.equal(pg.buffers["v"].cpu(), want))
+        check(f"graph v {it}", torch.equal(pg.buffers["v"].cpu(), want))
         want2 = torch.cat([torch.full((3 * 256,), float(-r - it)) for r in range(world)])
-        ok &= bool(torch.equal(pg.buffers["w"].cpu(), want2))
+        check(f"graph w {it}", torch.equal(pg.buffers["w"].cpu(), want2))
+        dist.barrier()
     # all-reduce with residual, interleaved with gathers on the same counters
     red_part = torch.empty(2048, device=dev)
     res = torch.empty(2048, device=dev)
@@ -103,7 +115,8 @@ def _gather_child(rank, world, port, out_dir):
         pg.allreduce("r", red_part, res, red_out)
         pg.gather("v", part)
         torch.cuda.synchronize(dev)
-        ok &= bool(torch.equal(red_out.cpu(), want_sum(ps, r0)))
+        check(f"eager all-reduce {it}", torch.equal(red_out.cpu(), want_sum(ps, r0)))
+        dist.barrier()
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2):
         pg.allreduce("r", red_part, res, red_out)
@@ -117,14 +130,15 @@ def _gather_child(rank, world, port, out_dir):
         torch.cuda.synchronize(dev)
         first = want_sum(ps, r0)
         # the second all-reduce sums every rank's first result (identical on all ranks)
-        ok &= bool(torch.equal(red_out.cpu(), first))
-        ok &= bool(torch.equal(red_out2.cpu(), want_sum([first] * world, r0)))
-    ok &= not pg.timed_out()
+        check(f"graph all-reduce {it}", torch.equal(red_out.cpu(), first))
+        check(f"graph all-reduce second {it}", torch.equal(red_out2.cpu(), want_sum([first] * world, r0)))
+        dist.barrier()
+    check("no wait ran out", not pg.timed_out())
     del g2
     del g
     pg.close()
     with open(os.path.join(out_dir, f"gather{rank}"), "w") as f:
-        f.write("ok" if ok else "bad")
+        f.write("ok" if not bad else "bad: " + ", ".join(bad))
     dist.barrier()
     dist.destroy_process_group()
 

@@ -1144,11 +1144,14 @@ struct AttnPlan {
     int splits;   // CTAs per KV head (grid x)
     int tpc;      // tokens per CTA (a multiple of 16)
     int records;  // partial records per query head in the workspace
-    bool per_sm;  // token-slice kernel in its per-SM shape (deep ring, no clusters)
+    bool per_sm;  // token-slice kernel in its per-SM shape (no clusters)
+    int stages;   // per-SM shape: ring stages (kFaDeepStages, or kAttStages to fit half an SM)
 };
 
 // Attention plan (vkc_set_attention_plan), per host thread: 0 chooses per
-// shape, 1 the clustered token-slice shape, 2 the per-SM shape.
+// shape, 1 the clustered token-slice shape, 2 the per-SM shape, 3 the per-SM
+// shape with a 3-stage ring (at most half an SM's shared memory, so a kernel
+// next to it in the stream can be resident beside it).
 thread_local int g_attn_plan = 0;
 
 int current_sm_count() {
@@ -1199,6 +1202,7 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
     t = ((t + 15) / 16) * 16;
     pl.tpc = t;
     pl.per_sm = false;
+    pl.stages = kAttStages;
     if (pl.kind == AttnPlan::kSlice) {
         pl.splits = target;
         pl.records = target / kFaCluster;
@@ -1218,8 +1222,9 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
         const int splits = (ctx + tpc - 1) / tpc;
         // automatic choice: the per-SM shape when it gives every CTA at least
         // two sub-tiles and keeps the grid in one wave
-        if (g_attn_plan == 2 || splits * n_kv <= current_sm_count()) {
+        if (g_attn_plan >= 2 || splits * n_kv <= current_sm_count()) {
             pl.per_sm = true;
+            pl.stages = g_attn_plan == 3 ? kAttStages : kFaDeepStages;
             pl.tpc = tpc;
             pl.splits = splits;
             pl.records = splits;
@@ -1298,8 +1303,18 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
         auto pick = [&](auto hd_tag) -> int {
             constexpr int HD = decltype(hd_tag)::value;
             cfg.blockDim = dim3(kFaThreads, 1, 1);
-            if (pl.per_sm) {
+            if (pl.per_sm && pl.stages == kFaDeepStages) {
                 constexpr int ST = kFaDeepStages;
+                const size_t smem = static_cast<size_t>(ST) * MmaGeo<HD>::SU * 16 + MmaGeo<HD>::q_bytes;
+                switch (G) {
+                    case 1: return go(attention_fa_kernel<1, HD, ST, 1>, smem);
+                    case 2: return go(attention_fa_kernel<2, HD, ST, 1>, smem);
+                    case 4: return go(attention_fa_kernel<4, HD, ST, 1>, smem);
+                    default: return go(attention_fa_kernel<8, HD, ST, 1>, smem);
+                }
+            }
+            if (pl.per_sm) {
+                constexpr int ST = kAttStages;
                 const size_t smem = static_cast<size_t>(ST) * MmaGeo<HD>::SU * 16 + MmaGeo<HD>::q_bytes;
                 switch (G) {
                     case 1: return go(attention_fa_kernel<1, HD, ST, 1>, smem);
@@ -1351,7 +1366,7 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx) {
 }
 
 int vkc_set_attention_plan(int plan) {
-    if (plan < 0 || plan > 2) return set_error(kErrArg, "attention plan %d (expected 0, 1 or 2)", plan);
+    if (plan < 0 || plan > 3) return set_error(kErrArg, "attention plan %d (expected 0 to 3)", plan);
     g_attn_plan = plan;
     return kOk;
 }

@@ -647,80 +647,99 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
 
     pdl_launch_dependents();
 
-    // ---- activations: gamma / scale / zero before the weight stream, x after
-    // the dependency wait; passes of 4096 values held in registers.
-    constexpr int kMaxAct = 4;
-    float av_g[kMaxAct], av_s[NS][kMaxAct], av_z[NS][kMaxAct], av_x[kMaxAct];
-    auto load_acts = [&](int base) {
+    // ---- activations, in passes of 4T values: in pass j thread tid holds the
+    // four consecutive k = j*4T + 4 tid .. + 3 (one 16-byte load per array), so
+    // a chunk row's KPC values sit in KPC/4 consecutive lanes and K (a multiple
+    // of KPC) ends on a row boundary.  gamma * scale and gamma * zero are formed
+    // before the dependency wait (they are weights); x is loaded after it.  The
+    // first kPre passes keep their activations in registers across the wait.
+    constexpr int kPass = 4 * kSmThreads;
+    constexpr int kPre = NS == 1 ? 3 : 1;
+    float4 gs[kPre][NS], gz[kPre][NS], xv[kPre];
+    auto mul4 = [](float4 a, float4 b) { return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); };
+    auto load_acts = [&](int j, float4 (&g_s)[NS], float4 (&g_z)[NS]) {
+        const int k = j * kPass + 4 * tid;
+        const bool ok = k < nk;
+        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (kNorm && ok) g = __ldg(reinterpret_cast<const float4*>(p.gamma + k));
 #pragma unroll
-        for (int q = 0; q < kMaxAct; ++q) {
-            const int k = base + tid + q * kSmThreads;
-            const bool ok = k < nk;
-            av_g[q] = (kNorm && ok) ? __ldg(p.gamma + k) : 1.f;
-#pragma unroll
-            for (int st = 0; st < NS; ++st) {
-                av_s[st][q] = (kQuant && ok) ? __ldg(p.s[st] + sblk + k) : 1.f;
-                av_z[st][q] = (kQuant && ok) ? __ldg(p.z[st] + sblk + k) : 0.f;
+        for (int st = 0; st < NS; ++st) {
+            if constexpr (kQuant) {
+                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                g_s[st] = ok ? mul4(g, __ldg(reinterpret_cast<const float4*>(p.s[st] + sblk + k))) : z4;
+                g_z[st] = ok ? mul4(g, __ldg(reinterpret_cast<const float4*>(p.z[st] + sblk + k))) : z4;
+            } else {
+                g_s[st] = g;
             }
         }
     };
-    auto load_x = [&](int base) {
-#pragma unroll
-        for (int q = 0; q < kMaxAct; ++q) {
-            const int k = base + tid + q * kSmThreads;
-            av_x[q] = k < nk ? p.x[k] : 0.f;
-        }
+    auto load_x = [&](int j) {
+        const int k = j * kPass + 4 * tid;
+        return k < nk ? *reinterpret_cast<const float4*>(p.x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
     };
     float ss = 0.f, cz[NS];
 #pragma unroll
     for (int st = 0; st < NS; ++st) cz[st] = 0.f;
-    auto fold = [&](int base) {
+    auto fold = [&](int j, const float4 x4, const float4 (&g_s)[NS], const float4 (&g_z)[NS]) {
+        const int k = j * kPass + 4 * tid;
+        const bool ok = k < nk;
+        if constexpr (kNorm) ss = fmaf(x4.x, x4.x, fmaf(x4.y, x4.y, fmaf(x4.z, x4.z, fmaf(x4.w, x4.w, ss))));
+        const int rl = k / KPC, i = k % KPC;  // i: a multiple of 4
 #pragma unroll
-        for (int q = 0; q < kMaxAct; ++q) {
-            // Lanes hold consecutive k (base and q*T are multiples of 32), so
-            // a chunk row's KPC values sit in KPC consecutive lanes, and K (a
-            // multiple of KPC) ends on a row boundary.
-            const int k = base + tid + q * kSmThreads;
-            const bool ok = k < nk;
-            const float xv = ok ? av_x[q] : 0.f;
-            float xg = xv;
-            if constexpr (kNorm) {
-                ss = fmaf(xv, xv, ss);
-                xg = xv * av_g[q];
-            }
-            const int rl = k / KPC, i = k % KPC;
+        for (int st = 0; st < NS; ++st) {
+            const float4 v = mul4(x4, g_s[st]);
+            if constexpr (kQuant)
+                cz[st] = fmaf(x4.x, g_z[st].x, fmaf(x4.y, g_z[st].y, fmaf(x4.z, g_z[st].z, fmaf(x4.w, g_z[st].w, cz[st]))));
+            const size_t b = static_cast<size_t>(rl * NS + st) * KPC;
+            if constexpr (kIdp) {
+                // x' of the row as integers of 16 bits against the row's
+                // largest magnitude m: X = rn(x' * 32767 / m), x' ~ X m / 32767
+                float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-            for (int st = 0; st < NS; ++st) {
-                float v = xg;
-                if constexpr (kQuant) {
-                    v = xg * av_s[st][q];
-                    cz[st] = fmaf(xg, av_z[st][q], cz[st]);
-                }
-                if constexpr (kIdp) {
-                    // x' of the row as integers of 16 bits against the row's
-                    // largest magnitude m: X = rn(x' * 32767 / m), x' ~ X m / 32767
-                    float m = fabsf(v);
-#pragma unroll
-                    for (int o = KPC / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                    const float inv = m > 0.f ? 32767.0f / m : 0.f;
-                    const int X = max(-32767, min(32767, __float2int_rn(v * inv)));
-                    if (ok) {
-                        // int8: byte i of the row; int4: the code word's even
-                        // nibbles (k = 8w + 0, 2, 4, 6) then its odd ones
-                        const int pos = BITS == 8 ? i : (((i >> 3) << 3) | ((i & 1) << 2) | ((i & 7) >> 1));
-                        const size_t b = static_cast<size_t>(rl * NS + st) * KPC + pos;
-                        xh[b] = static_cast<uint8_t>((X >> 8) & 0xFF);
-                        xl[b] = static_cast<uint8_t>(X & 0xFF);
-                        if (i == 0) xsig[rl * NS + st] = m * (1.0f / 32767.0f);
+                for (int o = KPC / 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float inv = m > 0.f ? __fdividef(32767.0f, m) : 0.f;
+                auto q16 = [&](float f) { return max(-32767, min(32767, __float2int_rn(f * inv))); };
+                const int X0 = q16(v.x), X1 = q16(v.y), X2 = q16(v.z), X3 = q16(v.w);
+                if (ok) {
+                    if constexpr (BITS == 8) {
+                        // bytes i .. i+3 of the row, in k order
+                        const uint32_t lo = (X0 & 0xFF) | ((X1 & 0xFF) << 8) | ((X2 & 0xFF) << 16) |
+                                            (static_cast<uint32_t>(X3 & 0xFF) << 24);
+                        const uint32_t hi = ((X0 >> 8) & 0xFF) | (((X1 >> 8) & 0xFF) << 8) |
+                                            (((X2 >> 8) & 0xFF) << 16) | (static_cast<uint32_t>((X3 >> 8) & 0xFF) << 24);
+                        *reinterpret_cast<uint32_t*>(xh + b + i) = hi;
+                        *reinterpret_cast<uint32_t*>(xl + b + i) = lo;
+                    } else {
+                        // int4: per code word (k = 8w + s) the even nibbles'
+                        // activations, then the odd ones: s -> ((s & 1) << 2) | (s >> 1).
+                        // Values s0..s0+3 (s0 = 0 or 4) go to bytes (s0/2, s0/2 + 1)
+                        // for s0, s0+2 and (4 + s0/2, 5 + s0/2) for s0+1, s0+3.
+                        const int w8 = (i >> 3) << 3, sh = (i & 4) >> 1;
+                        const uint32_t lo_e = (X0 & 0xFF) | ((X2 & 0xFF) << 8), lo_o = (X1 & 0xFF) | ((X3 & 0xFF) << 8);
+                        const uint32_t hi_e = ((X0 >> 8) & 0xFF) | (((X2 >> 8) & 0xFF) << 8);
+                        const uint32_t hi_o = ((X1 >> 8) & 0xFF) | (((X3 >> 8) & 0xFF) << 8);
+                        *reinterpret_cast<uint16_t*>(xh + b + w8 + sh) = static_cast<uint16_t>(hi_e);
+                        *reinterpret_cast<uint16_t*>(xh + b + w8 + 4 + sh) = static_cast<uint16_t>(hi_o);
+                        *reinterpret_cast<uint16_t*>(xl + b + w8 + sh) = static_cast<uint16_t>(lo_e);
+                        *reinterpret_cast<uint16_t*>(xl + b + w8 + 4 + sh) = static_cast<uint16_t>(lo_o);
                     }
-                } else if (ok) {
-                    if constexpr (BITS == 4) v *= int4_prescale(i);
-                    xs[(rl * NS + st) * KPC + i] = v;
+                    if (i == 0) xsig[rl * NS + st] = m * (1.0f / 32767.0f);
                 }
+            } else if (ok) {
+                float4 w = v;
+                if constexpr (BITS == 4) {
+                    w.x *= int4_prescale(i);
+                    w.y *= int4_prescale(i + 1);
+                    w.z *= int4_prescale(i + 2);
+                    w.w *= int4_prescale(i + 3);
+                }
+                *reinterpret_cast<float4*>(xs + b + i) = w;
             }
         }
     };
-    load_acts(0);
+#pragma unroll
+    for (int j = 0; j < kPre; ++j)
+        if (j * kPass < nk) load_acts(j, gs[j], gz[j]);
 
     // ---- weights: prime the ring with D rows per thread -------------------
     const int my_rows = streams && grp < p.R ? (p.R - grp + G - 1) / G : 0;  // rows grp, grp+G, ...
@@ -746,12 +765,15 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
 
     // ---- x depends on the previous kernel: wait for it, then fold --------
     pdl_wait();
-    load_x(0);
-    fold(0);
-    for (int base = kMaxAct * kSmThreads; base < nk; base += kMaxAct * kSmThreads) {
-        load_acts(base);
-        load_x(base);
-        fold(base);
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) xv[j] = j * kPass < nk ? load_x(j) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kPre; ++j)
+        if (j * kPass < nk) fold(j, xv[j], gs[j], gz[j]);
+    for (int j = kPre; j * kPass < nk; ++j) {
+        float4 g_s[NS], g_z[NS];
+        load_acts(j, g_s, g_z);
+        fold(j, load_x(j), g_s, g_z);
     }
     __syncthreads();
 
@@ -1363,13 +1385,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_batched_mma_kernel(const Bat
 struct DeviceInfo {
     int sms = 0;
 };
+constexpr int kMaxDevices = 64;
 std::mutex g_info_mu;
-DeviceInfo g_info[64];
+DeviceInfo g_info[kMaxDevices];
 
 int sm_count(int* out) {
     int dev = 0;
     VKC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return set_error(kErrUnsupported, "device ordinal %d", dev);
+    if (dev < 0 || dev >= kMaxDevices) return set_error(kErrUnsupported, "device ordinal %d", dev);
     std::lock_guard<std::mutex> lock(g_info_mu);
     if (g_info[dev].sms == 0)
         VKC_CUDA_TRY(cudaDeviceGetAttribute(&g_info[dev].sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1429,6 +1452,12 @@ SmShape sm_shape(int NS, int K, bool half) {
 template <int BITS, int MODE>
 bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh) {
     if (p.xslots || p.N % 2 != 0 || sh.smem > kSmMaxDynamicSmem) return false;
+    // activations are read as 16-byte vectors
+    auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (!aligned(p.x) || (MODE != kGemv && !aligned(p.gamma))) return false;
+    if (BITS <= 8)
+        for (int st = 0; st < (MODE == kSwiglu ? 2 : 1); ++st)
+            if (!aligned(p.s[st]) || !aligned(p.z[st])) return false;
     // every CTA gets at least one pair of outputs, and at most T - 2 outputs
     if (BITS <= 8 && (p.N / kGroup > sms || (sms + p.N / kGroup - 1) / (p.N / kGroup) > kGroup / 2)) return false;
     if (BITS > 8 && (p.N / 2 < sms || p.N / sms > sh.T - 2)) return false;
@@ -1446,11 +1475,14 @@ int launch_sm_shape_k(const GemvParams& p, cudaStream_t stream, int sms, size_t 
     if (int e = ensure_smem(kern, smem)) return e;
     if (T == 512) {
         // the largest shared-memory carveout, so that two CTAs fit on an SM
-        static bool carveout_set = false;
-        if (!carveout_set) {
+        // (a function attribute of each device's context)
+        static bool carveout_set[kMaxDevices] = {};
+        int dev = 0;
+        VKC_CUDA_TRY(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= kMaxDevices || !carveout_set[dev]) {
             VKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                               cudaSharedmemCarveoutMaxShared));
-            carveout_set = true;
+            if (dev >= 0 && dev < kMaxDevices) carveout_set[dev] = true;
         }
     }
     cudaLaunchConfig_t cfg = {};

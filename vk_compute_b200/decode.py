@@ -252,12 +252,27 @@ class ShardedDecoder:
     partial slots in peer-mapped memory, see p2p.PeerGather) or through
     torch.distributed (exchange="nccl"); either way a step can be captured in
     a CUDA graph.  Call close() before the process group is destroyed.
+
+    `shape` sets the CTA shapes of the step's kernels: "full" runs the GEMVs
+    as one 1024-thread CTA per SM and attention through a 6-stage ring (each
+    kernel owns the SMs); "half" keeps every kernel within half an SM (the
+    512-thread GEMV CTA, the 3-stage attention ring), so under programmatic
+    dependent launch each kernel becomes resident beside its predecessor and
+    streams its first weights or cache tiles while that one finishes.
     """
 
     EXCHANGES = ("p2p", "p2p-kernel", "nccl")
+    # (GEMV plan, attention plan) per shape.  With "full", a 512-thread GEMV
+    # CTA resident beside a clustered attention kernel would leave room for
+    # only one of its two CTAs per SM and split its grid into two waves.
+    SHAPES = {"full": ("auto-full", None), "half": ("per-sm-half", "per-sm-half")}
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
-                 group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p"):
+                 group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p", shape: str = "full"):
+        if shape not in self.SHAPES:
+            raise ValueError(f"shape {shape!r} (expected one of {tuple(self.SHAPES)})")
+        self.gemv_plan, self.attention_plan = self.SHAPES[shape]
+        self.shape = shape
         self.cfg = cfg
         self.plan = shard_plan(cfg, rank, world)
         self.device = torch.device(device or "cuda")
@@ -275,7 +290,7 @@ class ShardedDecoder:
         self.buf = Buffers(
             x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd),
             h=z(p.ffn_rows[1] - p.ffn_rows[0]), o_part=z(H), d_part=z(H),
-            ws=ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device))
+            ws=self._with_plans(lambda: ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device)))
         if self.exchange in ("p2p", "p2p-kernel"):
             from .p2p import PeerGather
 
@@ -314,19 +329,21 @@ class ShardedDecoder:
             self.peer.close()
             self.peer = None
 
-    # The GEMVs of a step run one 1024-thread CTA per SM (or clusters, for
-    # small shards): a 512-thread GEMV CTA resident beside the attention
-    # kernel would leave room for only one of its two CTAs per SM and split
-    # its clustered grid into two waves.
-    GEMV_PLAN = "auto-full"
+    def _with_plans(self, fn):
+        """fn() under this decoder's GEMV and attention plans (per host
+        thread), restoring the caller's afterwards."""
+        prev_g, prev_a = ops.get_gemv_plan(), ops.get_attention_plan()
+        ops.set_gemv_plan(self.gemv_plan)
+        if self.attention_plan is not None:
+            ops.set_attention_plan(self.attention_plan)
+        try:
+            return fn()
+        finally:
+            ops.set_gemv_plan(prev_g)
+            ops.set_attention_plan(prev_a)
 
     def step(self, pos: int) -> torch.Tensor:
-        prev = ops.get_gemv_plan()
-        ops.set_gemv_plan(self.GEMV_PLAN)
-        try:
-            return self._step(pos)
-        finally:
-            ops.set_gemv_plan(prev)
+        return self._with_plans(lambda: self._step(pos))
 
     def _step(self, pos: int) -> torch.Tensor:
         cfg, p, b = self.cfg, self.plan, self.buf
