@@ -541,14 +541,16 @@ def decode_parity(dec, cfg, rank: int, world: int, device, pos: int) -> dict | N
 
 
 def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float, parity: bool = True,
-                      shape: str = "full"):
+                      shape: str = "full", emulate_world: int = 1):
     """The 36-layer decoder chain (hidden 4096, 32 query / 8 KV heads of 128,
     intermediate 12288, int4 weights ~N(0,0.02), random-init) for one token at
     position 8191 (attention over a full 8192-token fp16 cache), sharded over
     `world` GPUs by heads (QKV, attention), input rows (O, down) and output
     rows (gate/up) with two all-reduces per layer (the library's NVLink peer
     all-reduce).  `shape` is the decoder's kernel shape (ShardedDecoder).
-    Steps are graph launches; time is the max over ranks."""
+    emulate_world > 1 (on one GPU) runs rank 0's shard of that many ranks
+    with no exchange: the compute share of a sharded step, without its
+    communication.  Steps are graph launches; time is the max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -556,7 +558,11 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
 
     cfg = DecoderConfig()
     t0 = time.perf_counter()
-    dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7, shape=shape)
+    if emulate_world > 1 and world == 1:
+        dec = ShardedDecoder(cfg, rank=0, world=emulate_world, device=device, seed=7, shape=shape, exchange="none")
+    else:
+        emulate_world = 1
+        dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7, shape=shape)
     pos = cfg.ctx - 1
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
@@ -597,7 +603,8 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
     kernels = dec.kernels_per_step()
     exchange = dec.exchange
     dec.close()
-    return {"layers": cfg.layers, "shape": shape, "us_per_step": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
+    extra = {"emulated_shard_of": emulate_world, "note": "rank 0's kernels only, no exchange"} if emulate_world > 1 else {}
+    return {**extra, "layers": cfg.layers, "shape": shape, "us_per_step": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
             "bytes_per_step": rank_bytes * world, "GB_s": round(rank_bytes * world / us / 1e3, 1),
             "frac_of_peak_per_gpu": round(rank_bytes / us / 1e3 / peak, 4),
             "kernels_per_step": kernels, "all_reduces_per_step": 2 * cfg.layers if world > 1 else 0,
@@ -760,7 +767,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-fma", action="store_true",
                     help="8/4-bit weights on the per-SM GEMV with fp32 FMAs instead of integer dot products")
-    ap.add_argument("--attention-plan", default="auto", choices=["auto", "clustered", "per-sm"],
+    ap.add_argument("--attention-plan", default="auto", choices=["auto", "clustered", "per-sm", "per-sm-half", "per-sm-x2"],
                     help="decode attention: chosen per shape, clusters of 8 CTAs per KV head, or one CTA per SM")
     ap.add_argument("--no-decode", action="store_true", help="skip the 36-layer decode-step measurement")
     ap.add_argument("--no-decode-parity", action="store_true",
@@ -768,7 +775,9 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config measurements beside the headline (N=1)")
     ap.add_argument("--decode-steps", type=int, default=20)
-    ap.add_argument("--decode-shape", default="full", choices=["full", "half"],
+    ap.add_argument("--decode-emulate-shard", type=int, default=1,
+                    help="on one GPU: time rank 0's share of an N-way sharded decode step, without exchanges")
+    ap.add_argument("--decode-shape", default="full", choices=["full", "half", "mixed"],
                     help="kernel shapes of the decode step (see ShardedDecoder)")
     ap.add_argument("--clock-window", type=float, default=1.5, help="seconds of sampled load before timing")
     args = ap.parse_args()
@@ -925,7 +934,8 @@ def main():
     if not args.no_decode:
         torch.cuda.synchronize()
         decode = decode_step_bench(rank, world, device, max(1, args.decode_steps), 3, peak,
-                                   parity=not args.no_decode_parity, shape=args.decode_shape)
+                                   parity=not args.no_decode_parity, shape=args.decode_shape,
+                                   emulate_world=args.decode_emulate_shard)
 
     configs = None
     if world == 1 and args.workload == "rmsnorm_gemv_int8" and not args.no_configs:

@@ -54,8 +54,8 @@ void vkc_set_timing(int enable);
 int vkc_get_timing(void);
 /* Which kernel runs the single-vector GEMV family (vkc_gemv,
  * vkc_rmsnorm_gemv, -rope, -rope_kv, -swiglu, vkc_gemv_residual / _peer):
- * 0 (default) chooses per shape -- one CTA per SM (512 threads for
- * single-stream fp16/fp32 weights, 1024 otherwise), each with a balanced range
+ * 0 (default) chooses per shape -- one CTA per SM (1024 threads for
+ * single-stream 4-bit weights, 512 otherwise), each with a balanced range
  * of whole-K output columns, when every SM gets at least 16 outputs and the
  * input is not a peer exchange; otherwise clusters that split K and reduce in
  * distributed shared memory.  1 always uses the cluster
@@ -221,8 +221,8 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
  * CTA per SM, each streaming a long token range through a deep ring, the
  * splits of a head merged by the last to finish; 3 the same with a 3-stage
  * ring in at most half an SM's shared memory (so the next kernel in the
- * stream can be resident beside it under programmatic dependent launch).
- * The workspace size
+ * stream can be resident beside it under programmatic dependent launch);
+ * 4 two such CTAs per SM over twice the splits.  The workspace size
  * (vkc_attention_workspace_bytes) depends on the plan in force.  No
  * counterpart in the reference. */
 int vkc_set_attention_plan(int plan);

@@ -14,7 +14,7 @@ from vk_compute_b200 import ops
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["clustered", "per-sm", "per-sm-half"])
+@pytest.fixture(autouse=True, params=["clustered", "per-sm", "per-sm-half", "per-sm-x2"])
 def attention_plan(request):
     """Every case runs under both splits of the cache for the token-slice
     kernel (head_dim 64/128): clusters of 8 CTAs per KV head, and at most one

@@ -275,6 +275,70 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, uint8_t* smem,
     if (tid == 0) p.tickets[kv] = 0u;
 }
 
+// The same merge for a record layout with at most NT float4 units per head
+// group (G * HD / 4 <= NT): the last CTA of the head gives each thread four
+// dimensions of one query head, and the thread folds the S records in order
+// with a running maximum (rescaling its sums when the maximum grows).  The
+// records are loaded 16 at a time into registers before any arithmetic, so
+// the merge costs one round trip to L2 per 16 splits rather than a staged
+// copy plus passes over shared memory.
+template <int G, int HD, int NT>
+__device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv, int S) {
+    static_assert(G * HD / 4 <= NT, "one float4 of one head per thread");
+    __shared__ unsigned s_ticket;
+    const int tid = threadIdx.x;
+    __threadfence();  // this CTA's record, before the ticket
+    __syncthreads();
+    if (tid == 0) s_ticket = atomicAdd(p.tickets + kv, 1u);
+    __syncthreads();
+    if (s_ticket != static_cast<unsigned>(S - 1)) return;
+    __threadfence();
+    if (tid < G * HD / 4) {
+        const int g = (4 * tid) / HD, d = 4 * tid - g * HD;
+        const int h = kv * G + g;
+        const float* rec = p.ws + static_cast<size_t>(h) * S * p.pitch;
+        float M = -INFINITY, L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        constexpr int kChunk = 16;
+        for (int s0 = 0; s0 < S; s0 += kChunk) {
+            float2 ml[kChunk];
+            float4 v[kChunk];
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                const float* r = rec + static_cast<size_t>(min(s0 + i, S - 1)) * p.pitch;
+                ml[i] = __ldcg(reinterpret_cast<const float2*>(r + HD));
+                v[i] = __ldcg(reinterpret_cast<const float4*>(r + d));
+            }
+            float Mc = M;
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i)
+                if (s0 + i < S) Mc = fmaxf(Mc, ml[i].x);
+            if (Mc == -INFINITY) continue;
+            const float f = M == -INFINITY ? 0.f : exp2f(M - Mc);
+            acc.x *= f;
+            acc.y *= f;
+            acc.z *= f;
+            acc.w *= f;
+            L *= f;
+            M = Mc;
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                if (s0 + i >= S || ml[i].x == -INFINITY) continue;
+                const float w = exp2f(ml[i].x - M);
+                L = fmaf(w, ml[i].y, L);
+                acc.x = fmaf(w, v[i].x, acc.x);
+                acc.y = fmaf(w, v[i].y, acc.y);
+                acc.z = fmaf(w, v[i].z, acc.z);
+                acc.w = fmaf(w, v[i].w, acc.w);
+            }
+        }
+        const float inv = 1.f / L;
+        *reinterpret_cast<float4*>(p.out + static_cast<size_t>(h) * HD + d) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+    if (tid == 0) p.tickets[kv] = 0u;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kAttThreads, 2) attention_decode_kernel(const AttnParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -876,17 +940,20 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
         ++s_pre;
     }
     pdl_wait();
-    for (int s = s_pre; s < ST; ++s) {
-        if (s < nsub) issue(s);
-        cp_commit();
-    }
 
     // q^T as B fragments in shared memory: entry (k-step, lane) =
     // {hi b0, hi b1, lo b0, lo b1}, b0 = q[gid][16 k + 2 t4 ..], b1 = +8.
-    for (int e = tid; e < KS * 32; e += kFaThreads) {
+    // q is loaded before the cache copies are issued, so its few loads are
+    // not queued behind this SM's ring of cache requests.
+    constexpr int QE = (KS * 32 + kFaThreads - 1) / kFaThreads;  // entries per thread
+    float qx[QE][4];
+#pragma unroll
+    for (int j = 0; j < QE; ++j) {
+        const int e = tid + j * kFaThreads;
         const int kj = e >> 5, g = (e & 31) >> 2, q4 = e & 3;
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
-        if (g < G) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qx[j][i] = 0.f;
+        if (e < KS * 32 && g < G) {
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const size_t qi = static_cast<size_t>(h0 + g) * HD + kj * 16 + half * 8 + 2 * q4;
@@ -895,14 +962,24 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
                     f = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(p.q) + qi));
                 else
                     f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(p.q) + qi);
-                x[2 * half] = f.x;
-                x[2 * half + 1] = f.y;
+                qx[j][2 * half] = f.x;
+                qx[j][2 * half + 1] = f.y;
             }
         }
-        uint4 fr;
-        split_pair(x[0], x[1], fr.x, fr.z);
-        split_pair(x[2], x[3], fr.y, fr.w);
-        qf[e] = fr;
+    }
+    for (int s = s_pre; s < ST; ++s) {
+        if (s < nsub) issue(s);
+        cp_commit();
+    }
+#pragma unroll
+    for (int j = 0; j < QE; ++j) {
+        const int e = tid + j * kFaThreads;
+        if (e < KS * 32) {
+            uint4 fr;
+            split_pair(qx[j][0], qx[j][1], fr.x, fr.z);
+            split_pair(qx[j][2], qx[j][3], fr.y, fr.w);
+            qf[e] = fr;
+        }
     }
     const bool q_lo = p.q_bits != 16;  // fp16 q has no low part
     // This lane's two heads (columns 2 t4, 2 t4 + 1) and whether they exist.
@@ -1058,6 +1135,28 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
         crec[tid * RP + HD] = M;
         crec[tid * RP + HD + 1] = L;
     }
+    if constexpr (CL == 1) {
+        // No cluster: the record goes straight to the workspace (or, with a
+        // single split, the normalised output to `out`).
+        __syncthreads();
+        if (p.splits == 1) {
+            for (int i = tid; i < G * HD; i += kFaThreads) {
+                const int g = i / HD, d = i - g * HD;
+                p.out[static_cast<size_t>(h0) * HD + i] = crec[g * RP + d] / crec[g * RP + HD + 1];
+            }
+            return;
+        }
+        for (int i = tid; i < G * RP / 4; i += kFaThreads) {
+            const int g = (4 * i) / RP, d = 4 * i - g * RP;
+            *reinterpret_cast<float4*>(p.ws + (static_cast<size_t>(h0 + g) * p.splits + split) * p.pitch + d) =
+                *reinterpret_cast<const float4*>(crec + g * RP + d);
+        }
+        if constexpr (G * HD / 4 <= kFaThreads)
+            merge_splits_direct<G, HD, kFaThreads>(p, kv, p.splits);
+        else
+            merge_splits<G, kFaThreads>(p, smem, kv, p.splits);
+        return;
+    }
 
     // ---- cluster of CL consecutive splits: rank 0 merges the records
     // of its peers through distributed shared memory.  Barrier 1 publishes the
@@ -1125,7 +1224,10 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
             r[0] = s_cM[tid];
             r[1] = s_cL[tid];
         }
-        merge_splits<G, kFaThreads>(p, smem, kv, nc);
+        if constexpr (G * HD / 4 <= kFaThreads)
+            merge_splits_direct<G, HD, kFaThreads>(p, kv, nc);
+        else
+            merge_splits<G, kFaThreads>(p, smem, kv, nc);
     }
     cluster_wait_acquire();
 }
@@ -1151,7 +1253,9 @@ struct AttnPlan {
 // Attention plan (vkc_set_attention_plan), per host thread: 0 chooses per
 // shape, 1 the clustered token-slice shape, 2 the per-SM shape, 3 the per-SM
 // shape with a 3-stage ring (at most half an SM's shared memory, so a kernel
-// next to it in the stream can be resident beside it).
+// next to it in the stream can be resident beside it), 4 two such CTAs per
+// SM over twice the splits (eight warps and the deep ring's bytes in flight
+// per SM).
 thread_local int g_attn_plan = 0;
 
 int current_sm_count() {
@@ -1215,7 +1319,8 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
         // least two sub-tiles, its range streamed through the deep ring; the
         // splits of a head merge through the workspace.
         const int tt = 8192 / hd;
-        const int per_head = current_sm_count() / n_kv > 0 ? current_sm_count() / n_kv : 1;
+        const int ctas = (g_attn_plan == 4 ? 2 : 1) * current_sm_count();
+        const int per_head = ctas / n_kv > 0 ? ctas / n_kv : 1;
         int tpc = (ctx + per_head - 1) / per_head;
         tpc = ((tpc + 15) / 16) * 16;
         if (tpc < 2 * tt) tpc = 2 * tt;
@@ -1224,7 +1329,7 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
         // two sub-tiles and keeps the grid in one wave
         if (g_attn_plan >= 2 || splits * n_kv <= current_sm_count()) {
             pl.per_sm = true;
-            pl.stages = g_attn_plan == 3 ? kAttStages : kFaDeepStages;
+            pl.stages = g_attn_plan >= 3 ? kAttStages : kFaDeepStages;
             pl.tpc = tpc;
             pl.splits = splits;
             pl.records = splits;
@@ -1366,7 +1471,7 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx) {
 }
 
 int vkc_set_attention_plan(int plan) {
-    if (plan < 0 || plan > 3) return set_error(kErrArg, "attention plan %d (expected 0 to 3)", plan);
+    if (plan < 0 || plan > 4) return set_error(kErrArg, "attention plan %d (expected 0 to 4)", plan);
     g_attn_plan = plan;
     return kOk;
 }

@@ -637,7 +637,9 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int col0, C;
-    sm_columns(p.N, kQuant, blockIdx.x, gridDim.x, col0, C);
+    // Reversed: the blocks split among one CTA more (the lighter CTAs) take
+    // the highest CTA indices, which start last and measured slowest.
+    sm_columns(p.N, kQuant, gridDim.x - 1 - blockIdx.x, gridDim.x, col0, C);
     const int G = kSmThreads / C;
     const int c = tid % C, grp = tid / C;
     const bool streams = grp < G;  // the last threads (fewer than C) only stage activations
@@ -1401,8 +1403,8 @@ int sm_count(int* out) {
 }
 
 // Which single-vector GEMV kernel runs (vkc_set_gemv_plan), per host thread:
-// 0 chooses per shape (the per-SM kernel's half-SM shape for single-stream
-// fp16/fp32 weights, its full-SM shape otherwise), 1 always the cluster
+// 0 chooses per shape (the per-SM kernel's full-SM shape for single-stream
+// 4-bit weights, its half-SM shape otherwise), 1 always the cluster
 // split-K kernel, 2 the one-CTA-per-SM kernel in its full-SM shape wherever it
 // can run, 3 the same in its half-SM shape, 4 chooses per shape with the
 // full-SM shape.
@@ -1527,10 +1529,11 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
     if (g_gemv_plan != 1) {
-        // automatic shape: 512 threads for single-stream fp16/fp32 weights
-        // (their FMA loop gains from the next launch's early ring), 1024
-        // threads for 8/4-bit weights and two streams (more bytes in flight)
-        const bool half = g_gemv_plan == 3 || (g_gemv_plan == 0 && BITS >= 16 && NS == 1);
+        // automatic shape, as measured on B200: 512 threads (the next launch
+        // primes its ring beside this one) except for single-stream 4-bit
+        // weights, whose short per-thread streams gain more from the 1024
+        // threads' bytes in flight
+        const bool half = g_gemv_plan == 3 || (g_gemv_plan == 0 && !(BITS == 4 && NS == 1));
         const SmShape sh = sm_shape(NS, p.K, half);
         if (sm_kernel_fits<BITS, MODE>(p, sms, sh)) return launch_sm<BITS, MODE>(p, stream, sms, sh);
     }

@@ -251,21 +251,27 @@ class ShardedDecoder:
     library's peer all-reduce kernel (exchange="p2p-kernel"; both keep the
     partial slots in peer-mapped memory, see p2p.PeerGather) or through
     torch.distributed (exchange="nccl"); either way a step can be captured in
-    a CUDA graph.  Call close() before the process group is destroyed.
+    a CUDA graph.  exchange="none" runs only this rank's own kernels, with no
+    exchange (the shard's partial sums stay local): a one-GPU stand-in for
+    timing one rank's share of a sharded step.  Call close() before the
+    process group is destroyed.
 
     `shape` sets the CTA shapes of the step's kernels: "full" runs the GEMVs
     as one 1024-thread CTA per SM and attention through a 6-stage ring (each
     kernel owns the SMs); "half" keeps every kernel within half an SM (the
     512-thread GEMV CTA, the 3-stage attention ring), so under programmatic
     dependent launch each kernel becomes resident beside its predecessor and
-    streams its first weights or cache tiles while that one finishes.
+    streams its first weights or cache tiles while that one finishes; "mixed"
+    runs the GEMVs in half an SM (four consecutive GEMVs per layer overlap
+    pairwise) and attention through the 6-stage ring.
     """
 
-    EXCHANGES = ("p2p", "p2p-kernel", "nccl")
+    EXCHANGES = ("p2p", "p2p-kernel", "nccl", "none")
     # (GEMV plan, attention plan) per shape.  With "full", a 512-thread GEMV
     # CTA resident beside a clustered attention kernel would leave room for
     # only one of its two CTAs per SM and split its grid into two waves.
-    SHAPES = {"full": ("auto-full", None), "half": ("per-sm-half", "per-sm-half")}
+    SHAPES = {"full": ("auto-full", None), "half": ("per-sm-half", "per-sm-half"),
+              "mixed": ("per-sm-half", "per-sm")}
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
                  group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p", shape: str = "full"):
@@ -352,7 +358,7 @@ class ShardedDecoder:
         hd = cfg.head_dim
         q_rows, kv_rows = p.n_q * hd, p.n_kv * hd
         scale = 1.0 / math.sqrt(hd)
-        single = p.world == 1
+        single = p.world == 1 or self.exchange == "none"
         fused = self.exchange == "p2p"
         last = len(self.layers) - 1
         for li, L in enumerate(self.layers):

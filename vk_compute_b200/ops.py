@@ -417,14 +417,15 @@ def get_gemv_int_dot() -> bool:
     return bool(lib().vkc_get_gemv_int_dot())
 
 
-ATTENTION_PLANS = {"auto": 0, "clustered": 1, "per-sm": 2, "per-sm-half": 3}
+ATTENTION_PLANS = {"auto": 0, "clustered": 1, "per-sm": 2, "per-sm-half": 3, "per-sm-x2": 4}
 
 
 def set_attention_plan(plan: str) -> None:
     """Decode attention's split of the cache (vkc_set_attention_plan):
     "auto" per shape, "clustered" (clusters of 8 CTAs per KV head, two CTAs
     per SM), "per-sm" (at most one CTA per SM, deep ring), "per-sm-half" (the
-    same with a 3-stage ring in at most half an SM).  Per host thread."""
+    same with a 3-stage ring in at most half an SM), "per-sm-x2" (two such
+    CTAs per SM over twice the splits).  Per host thread."""
     check(lib().vkc_set_attention_plan(ATTENTION_PLANS[plan]))
 
 
