@@ -541,7 +541,7 @@ def decode_parity(dec, cfg, rank: int, world: int, device, pos: int) -> dict | N
 
 
 def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, peak: float, parity: bool = True,
-                      shape: str = "full", emulate_world: int = 1):
+                      shape: str = "full", emulate_world: int = 1, exchange: str = "p2p"):
     """The 36-layer decoder chain (hidden 4096, 32 query / 8 KV heads of 128,
     intermediate 12288, int4 weights ~N(0,0.02), random-init) for one token at
     position 8191 (attention over a full 8192-token fp16 cache), sharded over
@@ -562,7 +562,7 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
         dec = ShardedDecoder(cfg, rank=0, world=emulate_world, device=device, seed=7, shape=shape, exchange="none")
     else:
         emulate_world = 1
-        dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7, shape=shape)
+        dec = ShardedDecoder(cfg, rank=rank, world=world, device=device, seed=7, shape=shape, exchange=exchange)
     pos = cfg.ctx - 1
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
@@ -610,7 +610,9 @@ def decode_step_bench(rank: int, world: int, device, steps: int, warmup: int, pe
             "kernels_per_step": kernels, "all_reduces_per_step": 2 * cfg.layers if world > 1 else 0,
             "steps": steps, "warmup": warmup, "pos": pos, "ctx": cfg.ctx,
             "parallelism": (f"head/K-split shards x{world}, all-reduce x2 per layer ({exchange}: "
-                            + ("NVLink peer stores" if exchange == "p2p" else "NCCL") + ")") if world > 1 else "1 GPU",
+                            + {"p2p": "NVLink peer stores fused into the projections",
+                               "p2p-kernel": "NVLink peer all-reduce kernel",
+                               "nccl": "NCCL all-reduce"}.get(exchange, exchange) + ")") if world > 1 else "1 GPU",
             "build_s": round(build_s, 1),
             "parity": check,
             "model": "36 x (RmsNorm-GEMV-Rope QKV 6144x4096 + KV append, Att-full GQA 32/8 x 128, "
@@ -767,7 +769,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-fma", action="store_true",
                     help="8/4-bit weights on the per-SM GEMV with fp32 FMAs instead of integer dot products")
-    ap.add_argument("--attention-plan", default="auto", choices=["auto", "clustered", "per-sm", "per-sm-half", "per-sm-x2"],
+    ap.add_argument("--attention-plan", default="auto", choices=["auto", "clustered", "per-sm", "per-sm-half", "per-sm-x2", "per-sm-wide"],
                     help="decode attention: chosen per shape, clusters of 8 CTAs per KV head, or one CTA per SM")
     ap.add_argument("--no-decode", action="store_true", help="skip the 36-layer decode-step measurement")
     ap.add_argument("--no-decode-parity", action="store_true",
@@ -775,6 +777,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config measurements beside the headline (N=1)")
     ap.add_argument("--decode-steps", type=int, default=20)
+    ap.add_argument("--decode-exchange", default="p2p", choices=["p2p", "p2p-kernel", "nccl"],
+                    help="how the sharded decode step sums the K-split projections across ranks")
     ap.add_argument("--decode-emulate-shard", type=int, default=1,
                     help="on one GPU: time rank 0's share of an N-way sharded decode step, without exchanges")
     ap.add_argument("--decode-shape", default="full", choices=["full", "half", "mixed"],
@@ -935,7 +939,7 @@ def main():
         torch.cuda.synchronize()
         decode = decode_step_bench(rank, world, device, max(1, args.decode_steps), 3, peak,
                                    parity=not args.no_decode_parity, shape=args.decode_shape,
-                                   emulate_world=args.decode_emulate_shard)
+                                   emulate_world=args.decode_emulate_shard, exchange=args.decode_exchange)
 
     configs = None
     if world == 1 and args.workload == "rmsnorm_gemv_int8" and not args.no_configs:

@@ -222,11 +222,20 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx);
  * splits of a head merged by the last to finish; 3 the same with a 3-stage
  * ring in at most half an SM's shared memory (so the next kernel in the
  * stream can be resident beside it under programmatic dependent launch);
- * 4 two such CTAs per SM over twice the splits.  The workspace size
+ * 4 two such CTAs per SM over twice the splits; 5 the per-SM shape with
+ * two warp groups per CTA working on alternate sub-tiles (what 0 uses
+ * wherever the per-SM shape applies).  The workspace size
  * (vkc_attention_workspace_bytes) depends on the plan in force.  No
  * counterpart in the reference. */
 int vkc_set_attention_plan(int plan);
 int vkc_get_attention_plan(void);
+/* The split decode attention would use for a shape under the calling
+ * thread's plan: info[0] kernel (1 token-slice clustered, 2 token-slice
+ * per-SM, 3 head_dim-256 tensor-core, 4 SIMT), [1] CTAs per KV head, [2]
+ * tokens per CTA, [3] ring stages, [4] warp groups per CTA, [5] CTAs per
+ * cluster, [6] partial records per query head.  No counterpart in the
+ * reference. */
+int vkc_attention_plan_info(int n_q, int n_kv, int head_dim, int ctx, int* info);
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                          void* workspace, size_t workspace_bytes, void* stream);

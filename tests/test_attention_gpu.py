@@ -14,7 +14,7 @@ from vk_compute_b200 import ops
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["clustered", "per-sm", "per-sm-half", "per-sm-x2"])
+@pytest.fixture(autouse=True, params=["auto", "clustered", "per-sm", "per-sm-half", "per-sm-x2", "per-sm-wide"])
 def attention_plan(request):
     """Every case runs under both splits of the cache for the token-slice
     kernel (head_dim 64/128): clusters of 8 CTAs per KV head, and at most one
@@ -137,3 +137,20 @@ def test_append_variant_matches(n_q, n_kv, hd, ctx):
     finally:
         ops.set_pdl(prev)
     assert torch.equal(a, b)
+
+
+def test_plan_info_matches_plan(request):
+    """The plan query names the split the launch uses; the per-SM shapes keep
+    the grid within one wave of the SMs."""
+    plan = ops.get_attention_plan()
+    info = ops.attention_plan_info(32, 8, 128, 8192)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if plan == "clustered":
+        assert info["kernel"] == "token-slice clustered" and info["cluster"] == 8
+        return
+    assert info["kernel"] == "token-slice per-SM"
+    assert info["splits"] * info["tokens_per_cta"] >= 8192
+    ctas_per_sm = 2 if plan == "per-sm-x2" else 1
+    assert info["splits"] * 8 <= ctas_per_sm * sms
+    if plan in ("per-sm-wide", "auto"):
+        assert info["warp_groups"] == 2

@@ -279,8 +279,8 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, uint8_t* smem,
 // group (G * HD / 4 <= NT): the last CTA of the head gives each thread four
 // dimensions of one query head, and the thread folds the S records in order
 // with a running maximum (rescaling its sums when the maximum grows).  The
-// records are loaded 16 at a time into registers before any arithmetic, so
-// the merge costs one round trip to L2 per 16 splits rather than a staged
+// records are loaded 24 at a time into registers before any arithmetic, so
+// the merge costs one round trip to L2 per 24 splits rather than a staged
 // copy plus passes over shared memory.
 template <int G, int HD, int NT>
 __device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv, int S) {
@@ -299,7 +299,7 @@ __device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv,
         const float* rec = p.ws + static_cast<size_t>(h) * S * p.pitch;
         float M = -INFINITY, L = 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        constexpr int kChunk = 16;
+        constexpr int kChunk = 24;
         for (int s0 = 0; s0 < S; s0 += kChunk) {
             float2 ml[kChunk];
             float4 v[kChunk];
@@ -876,16 +876,18 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     return y;
 }
 
-template <int G, int HD, int ST, int CL>
-__global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kernel(const AttnParams p) {
+template <int G, int HD, int ST, int CL, int NWG = 1>
+__global__ void __launch_bounds__(kFaThreads * NWG, ST > 3 ? 1 : 2) attention_fa_kernel(const AttnParams p) {
     using Geo = MmaGeo<HD>;
     constexpr int CH = Geo::CH, TT = Geo::TT, KROW = Geo::KROW, VROW = Geo::VROW, KU = Geo::KU, SU = Geo::SU;
-    constexpr int NW = kFaThreads / 32;    // warps
-    constexpr int SPW = TT / (16 * NW);    // 16-token slices per warp per sub-tile
+    constexpr int NT = kFaThreads * NWG;   // threads: NWG warp groups of kFaThreads
+    constexpr int NW = NT / 32;            // warps
+    constexpr int SPW = TT / (16 * (kFaThreads / 32));  // 16-token slices per warp per sub-tile
     constexpr int KS = HD / 16;            // score k-steps
     constexpr int MT = HD / 16;            // P.V m-tiles of 16 dimensions
     constexpr int CPT = 1024 / kFaThreads; // K (and V) copies per thread per sub-tile
-    static_assert(SPW >= 1 && TT % (16 * NW) == 0 && KS % 2 == 0, "geometry");
+    static_assert(SPW >= 1 && TT % (16 * (kFaThreads / 32)) == 0 && KS % 2 == 0, "geometry");
+    static_assert(ST % NWG == 0 && (NWG == 1 || CL == 1), "warp groups take every NWG-th stage; no clusters");
     static_assert(kFaThreads % CH == 0 && kFaThreads % TT == 0, "copy plan");
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_wm[NW][8], s_wl[NW][8];
@@ -893,6 +895,15 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
     const int split = blockIdx.x, kv = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gid = lane >> 2, t4 = lane & 3;
+    // Warp group wg streams and processes the sub-tiles s = wg, wg + NWG, ...
+    // through the ring stages s % ST, with its own copy groups and barrier.
+    const int wg = tid / kFaThreads, ltid = tid % kFaThreads, lwarp = warp % (kFaThreads / 32);
+    auto group_sync = [&]() {
+        if constexpr (NWG == 1)
+            __syncthreads();
+        else
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + wg), "n"(kFaThreads) : "memory");
+    };
     const int t0 = split * p.tpc;
     const int T = min(p.tpc, p.ctx - t0);
     const int nsub = (T + TT - 1) / TT;
@@ -903,10 +914,10 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
 
     pdl_launch_dependents();
 
-    // Copy plan: K chunk tid % CH of tokens tid / CH + i (128 / CH); V token
-    // tid % TT of chunks tid / TT + i (128 / TT); i < CPT.
-    const int k_tok = tid / CH, k_chk = tid % CH;
-    const int v_tok = tid % TT, v_chk = tid / TT;
+    // Copy plan (per warp group): K chunk ltid % CH of tokens ltid / CH + i
+    // (128 / CH); V token ltid % TT of chunks ltid / TT + i (128 / TT); i < CPT.
+    const int k_tok = ltid / CH, k_chk = ltid % CH;
+    const int v_tok = ltid % TT, v_chk = ltid / TT;
     const uint4* k_src0 = p.kc + (static_cast<size_t>(t0 + k_tok) * p.n_kv + kv) * CH + k_chk;
     const size_t k_step = static_cast<size_t>(kFaThreads / CH) * p.n_kv * CH;
     const uint4* v_src0 = p.vc + (static_cast<size_t>(kv) * CH + v_chk) * p.ctx_cap + t0 + v_tok;
@@ -933,11 +944,11 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
     // Sub-tiles whose tokens all lie below p.stable (cache rows no kernel still
     // in flight writes) are requested before the wait on the previous kernel;
     // the rest, and q, after it.  Commit groups stay in sub-tile order.
-    int s_pre = 0;
+    int s_pre = wg;
     while (s_pre < ST && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable) {
         issue(s_pre);
         cp_commit();
-        ++s_pre;
+        s_pre += NWG;
     }
     pdl_wait();
 
@@ -945,11 +956,11 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
     // {hi b0, hi b1, lo b0, lo b1}, b0 = q[gid][16 k + 2 t4 ..], b1 = +8.
     // q is loaded before the cache copies are issued, so its few loads are
     // not queued behind this SM's ring of cache requests.
-    constexpr int QE = (KS * 32 + kFaThreads - 1) / kFaThreads;  // entries per thread
+    constexpr int QE = (KS * 32 + NT - 1) / NT;  // entries per thread
     float qx[QE][4];
 #pragma unroll
     for (int j = 0; j < QE; ++j) {
-        const int e = tid + j * kFaThreads;
+        const int e = tid + j * NT;
         const int kj = e >> 5, g = (e & 31) >> 2, q4 = e & 3;
 #pragma unroll
         for (int i = 0; i < 4; ++i) qx[j][i] = 0.f;
@@ -967,13 +978,13 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
             }
         }
     }
-    for (int s = s_pre; s < ST; ++s) {
+    for (int s = s_pre; s < ST; s += NWG) {
         if (s < nsub) issue(s);
         cp_commit();
     }
 #pragma unroll
     for (int j = 0; j < QE; ++j) {
-        const int e = tid + j * kFaThreads;
+        const int e = tid + j * NT;
         if (e < KS * 32) {
             uint4 fr;
             split_pair(qx[j][0], qx[j][1], fr.x, fr.z);
@@ -992,14 +1003,15 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
 
-    for (int s = 0; s < nsub; ++s) {
-        cp_wait<ST - 1>();
-        __syncthreads();  // sub-tile s landed for all threads (and q fragments, first time)
+    if constexpr (NWG > 1) __syncthreads();  // q fragments of all groups
+    for (int s = wg; s < nsub; s += NWG) {
+        cp_wait<ST / NWG - 1>();
+        group_sync();  // sub-tile s landed for the group's threads (and q fragments, first time)
         const uint32_t base = smem_addr(ring + (s % ST) * SU);
         const int nt = min(TT, T - s * TT);
 #pragma unroll
         for (int sl = 0; sl < SPW; ++sl) {
-            const int ts0 = (warp * SPW + sl) * 16;  // first token of the slice
+            const int ts0 = (lwarp * SPW + sl) * 16;  // first token of the slice
 
             // scores S^T; two accumulators (even / odd k-steps) halve the MMA chain
             float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1069,7 +1081,7 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
                 mma16816_full(acc[mt], a, bl0, bl1);
             }
         }
-        __syncthreads();  // slot of sub-tile s consumed by all warps
+        group_sync();  // slot of sub-tile s consumed by the group's warps
         if (s + ST < nsub) issue(s + ST);
         cp_commit();
     }
@@ -1115,7 +1127,7 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
     // This CTA's record in shared memory, [G][HD + 4]: acc[HD], m, l.
     constexpr int RP = HD + 4;
     float* crec = red + NW * G * HD;
-    for (int i = tid; i < G * HD; i += kFaThreads) {
+    for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, d = i - g * HD;
         float x = 0.f;
 #pragma unroll
@@ -1140,21 +1152,21 @@ __global__ void __launch_bounds__(kFaThreads, ST > 3 ? 1 : 2) attention_fa_kerne
         // single split, the normalised output to `out`).
         __syncthreads();
         if (p.splits == 1) {
-            for (int i = tid; i < G * HD; i += kFaThreads) {
+            for (int i = tid; i < G * HD; i += NT) {
                 const int g = i / HD, d = i - g * HD;
                 p.out[static_cast<size_t>(h0) * HD + i] = crec[g * RP + d] / crec[g * RP + HD + 1];
             }
             return;
         }
-        for (int i = tid; i < G * RP / 4; i += kFaThreads) {
+        for (int i = tid; i < G * RP / 4; i += NT) {
             const int g = (4 * i) / RP, d = 4 * i - g * RP;
             *reinterpret_cast<float4*>(p.ws + (static_cast<size_t>(h0 + g) * p.splits + split) * p.pitch + d) =
                 *reinterpret_cast<const float4*>(crec + g * RP + d);
         }
-        if constexpr (G * HD / 4 <= kFaThreads)
-            merge_splits_direct<G, HD, kFaThreads>(p, kv, p.splits);
+        if constexpr (G * HD / 4 <= NT)
+            merge_splits_direct<G, HD, NT>(p, kv, p.splits);
         else
-            merge_splits<G, kFaThreads>(p, smem, kv, p.splits);
+            merge_splits<G, NT>(p, smem, kv, p.splits);
         return;
     }
 
@@ -1248,6 +1260,7 @@ struct AttnPlan {
     int records;  // partial records per query head in the workspace
     bool per_sm;  // token-slice kernel in its per-SM shape (no clusters)
     int stages;   // per-SM shape: ring stages (kFaDeepStages, or kAttStages to fit half an SM)
+    int groups;   // per-SM shape: warp groups of kFaThreads per CTA
 };
 
 // Attention plan (vkc_set_attention_plan), per host thread: 0 chooses per
@@ -1255,7 +1268,12 @@ struct AttnPlan {
 // shape with a 3-stage ring (at most half an SM's shared memory, so a kernel
 // next to it in the stream can be resident beside it), 4 two such CTAs per
 // SM over twice the splits (eight warps and the deep ring's bytes in flight
-// per SM).
+// per SM), 5 the per-SM shape with two warp groups per CTA, each streaming
+// and processing alternate sub-tiles of the CTA's range through its half of
+// the deep ring (eight warps per SM, one record per CTA).  The automatic
+// choice is 5 wherever the per-SM shape applies.  (Per-SM CTAs in clusters
+// of 8 were measured too: B200's GPCs hold too few such clusters at once,
+// and the grid ran in two waves.)
 thread_local int g_attn_plan = 0;
 
 int current_sm_count() {
@@ -1307,6 +1325,7 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
     pl.tpc = t;
     pl.per_sm = false;
     pl.stages = kAttStages;
+    pl.groups = 1;
     if (pl.kind == AttnPlan::kSlice) {
         pl.splits = target;
         pl.records = target / kFaCluster;
@@ -1329,7 +1348,8 @@ static AttnPlan attention_plan(int n_q, int n_kv, int hd, int ctx) {
         // two sub-tiles and keeps the grid in one wave
         if (g_attn_plan >= 2 || splits * n_kv <= current_sm_count()) {
             pl.per_sm = true;
-            pl.stages = g_attn_plan >= 3 ? kAttStages : kFaDeepStages;
+            pl.stages = g_attn_plan == 3 || g_attn_plan == 4 ? kAttStages : kFaDeepStages;
+            pl.groups = g_attn_plan == 5 || g_attn_plan == 0 ? 2 : 1;
             pl.tpc = tpc;
             pl.splits = splits;
             pl.records = splits;
@@ -1408,6 +1428,17 @@ int attention_launch(const void* q, int q_bits, const void* kc, const void* vc, 
         auto pick = [&](auto hd_tag) -> int {
             constexpr int HD = decltype(hd_tag)::value;
             cfg.blockDim = dim3(kFaThreads, 1, 1);
+            if (pl.per_sm && pl.groups == 2) {
+                constexpr int ST = kFaDeepStages;
+                cfg.blockDim = dim3(2 * kFaThreads, 1, 1);
+                const size_t smem = static_cast<size_t>(ST) * MmaGeo<HD>::SU * 16 + MmaGeo<HD>::q_bytes;
+                switch (G) {
+                    case 1: return go(attention_fa_kernel<1, HD, ST, 1, 2>, smem);
+                    case 2: return go(attention_fa_kernel<2, HD, ST, 1, 2>, smem);
+                    case 4: return go(attention_fa_kernel<4, HD, ST, 1, 2>, smem);
+                    default: return go(attention_fa_kernel<8, HD, ST, 1, 2>, smem);
+                }
+            }
             if (pl.per_sm && pl.stages == kFaDeepStages) {
                 constexpr int ST = kFaDeepStages;
                 const size_t smem = static_cast<size_t>(ST) * MmaGeo<HD>::SU * 16 + MmaGeo<HD>::q_bytes;
@@ -1471,11 +1502,26 @@ size_t vkc_attention_workspace_bytes(int n_q, int n_kv, int head_dim, int ctx) {
 }
 
 int vkc_set_attention_plan(int plan) {
-    if (plan < 0 || plan > 4) return set_error(kErrArg, "attention plan %d (expected 0 to 4)", plan);
+    if (plan < 0 || plan > 5) return set_error(kErrArg, "attention plan %d (expected 0 to 5)", plan);
     g_attn_plan = plan;
     return kOk;
 }
 int vkc_get_attention_plan(void) { return g_attn_plan; }
+
+int vkc_attention_plan_info(int n_q, int n_kv, int head_dim, int ctx, int* info) {
+    if (!info) return set_error(kErrArg, "null info");
+    if (n_q <= 0 || n_kv <= 0 || n_q % n_kv != 0 || head_dim <= 0 || ctx <= 0)
+        return set_error(kErrArg, "bad attention shape");
+    const AttnPlan pl = attention_plan(n_q, n_kv, head_dim, ctx);
+    info[0] = pl.kind == AttnPlan::kSlice ? (pl.per_sm ? 2 : 1) : pl.kind == AttnPlan::kMma ? 3 : 4;
+    info[1] = pl.splits;
+    info[2] = pl.tpc;
+    info[3] = pl.per_sm ? pl.stages : kAttStages;
+    info[4] = pl.per_sm ? pl.groups : 1;
+    info[5] = pl.kind == AttnPlan::kSlice && !pl.per_sm ? kFaCluster : 1;
+    info[6] = pl.records;
+    return kOk;
+}
 
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,

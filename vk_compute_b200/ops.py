@@ -417,7 +417,7 @@ def get_gemv_int_dot() -> bool:
     return bool(lib().vkc_get_gemv_int_dot())
 
 
-ATTENTION_PLANS = {"auto": 0, "clustered": 1, "per-sm": 2, "per-sm-half": 3, "per-sm-x2": 4}
+ATTENTION_PLANS = {"auto": 0, "clustered": 1, "per-sm": 2, "per-sm-half": 3, "per-sm-x2": 4, "per-sm-wide": 5}
 
 
 def set_attention_plan(plan: str) -> None:
@@ -425,13 +425,27 @@ def set_attention_plan(plan: str) -> None:
     "auto" per shape, "clustered" (clusters of 8 CTAs per KV head, two CTAs
     per SM), "per-sm" (at most one CTA per SM, deep ring), "per-sm-half" (the
     same with a 3-stage ring in at most half an SM), "per-sm-x2" (two such
-    CTAs per SM over twice the splits).  Per host thread."""
+    CTAs per SM over twice the splits), "per-sm-wide" (the per-SM shape with
+    two warp groups per CTA on alternate sub-tiles; the automatic choice
+    wherever the per-SM shape applies).  Per host thread."""
     check(lib().vkc_set_attention_plan(ATTENTION_PLANS[plan]))
 
 
 def get_attention_plan() -> str:
     v = lib().vkc_get_attention_plan()
     return next(k for k, n in ATTENTION_PLANS.items() if n == v)
+
+
+def attention_plan_info(n_q: int, n_kv: int, head_dim: int, ctx: int) -> dict:
+    """The split decode attention uses for a shape under the calling thread's
+    plan (vkc_attention_plan_info)."""
+    import ctypes as C
+
+    info = (C.c_int * 7)()
+    check(lib().vkc_attention_plan_info(n_q, n_kv, head_dim, ctx, info))
+    kinds = {1: "token-slice clustered", 2: "token-slice per-SM", 3: "tensor-core hd256", 4: "SIMT"}
+    return {"kernel": kinds[info[0]], "splits": info[1], "tokens_per_cta": info[2], "stages": info[3],
+            "warp_groups": info[4], "cluster": info[5], "records": info[6]}
 
 
 def get_gemv_plan() -> str:
