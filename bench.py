@@ -781,7 +781,7 @@ def main():
                     help="how the sharded decode step sums the K-split projections across ranks")
     ap.add_argument("--decode-emulate-shard", type=int, default=1,
                     help="on one GPU: time rank 0's share of an N-way sharded decode step, without exchanges")
-    ap.add_argument("--decode-shape", default="full", choices=["full", "half", "mixed"],
+    ap.add_argument("--decode-shape", default="full", choices=["full", "half", "mixed", "persistent"],
                     help="kernel shapes of the decode step (see ShardedDecoder)")
     ap.add_argument("--clock-window", type=float, default=1.5, help="seconds of sampled load before timing")
     args = ap.parse_args()

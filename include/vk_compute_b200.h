@@ -83,8 +83,9 @@ int vkc_has_operator(const char* shader);
  * record a bounded device wait that gave up (the kernel then ends early and
  * its outputs are invalid): 0x1 a producer warp, 0x2 a consumer warp, 0x4 a
  * cluster's collecting CTA (split-K deposits), 0x8 a wait for another GPU's
- * data (peer timeout).  `clear` resets the word.  No counterpart in the
- * reference. */
+ * data (peer timeout), 0x20 a grid-barrier wait of the persistent decoder
+ * (the tcgen05 GEMM keeps its own word, flag 0x10).  `clear` resets the word.
+ * No counterpart in the reference. */
 int vkc_device_status(unsigned* status, int clear);
 /* Bounds of those waits, in nanoseconds of the GPU clock: `peer_ns`, the
  * longest one thread waits in total for other GPUs' data in a fused exchange
@@ -236,6 +237,47 @@ int vkc_get_attention_plan(void);
  * cluster, [6] partial records per query head.  No counterpart in the
  * reference. */
 int vkc_attention_plan_info(int n_q, int n_kv, int head_dim, int ctx, int* info);
+
+/* The decoder step as one persistent kernel (one GPU, 4-bit weights, four
+ * query heads per KV head, head_dim 64 or 128).  Per layer it runs, separated
+ * by grid-wide barriers instead of kernel boundaries: RMSNorm-QKV-RoPE with
+ * the KV append (rows [Q | K0 V0 | K1 V1 | ...], theta per rotary pair),
+ * attention over tokens [0, pos], x' = x + O attn, h = RMSNorm-SwiGLU(x'),
+ * x = x' + down h -- the arithmetic of vkc_rmsnorm_gemv_rope_kv,
+ * vkc_attention_decode, vkc_gemv_residual and vkc_rmsnorm_swiglu.  Each phase
+ * requests its weights before it waits at the barrier.  A barrier wait that
+ * runs out (kGridWaitNs, the peer-exchange limit) sets status flag 0x20 and
+ * the launch gives up waiting.  The launch is cooperative (all CTAs resident;
+ * it fails with an error where the device cannot hold them).
+ * `program` (vkc_decode_program_bytes, 256-byte aligned device memory) holds
+ * the per-layer parameters, the barrier counter and the attention workspace;
+ * build it once per set of weights and buffers, then run it per token (runs
+ * on one stream do not overlap).  No counterpart in the reference. */
+typedef struct vkc_decode_dims {
+    int layers, hidden, inter, n_q, n_kv, head_dim, ctx_cap, bits;
+    float eps;
+} vkc_decode_dims;
+typedef struct vkc_decode_layer {
+    const void* qkv; const float* qkv_scale; const float* qkv_zero;
+    const void* o; const float* o_scale; const float* o_zero;
+    const void* gate; const float* gate_scale; const float* gate_zero;
+    const void* up; const float* up_scale; const float* up_zero;
+    const void* down; const float* down_scale; const float* down_zero;
+    const float* gamma_attn; const float* gamma_ffn;
+    void* kcache; void* vcache;  /* fp16, the layouts of vkc_attention_decode */
+} vkc_decode_layer;
+typedef struct vkc_decode_buffers {
+    float* x;      /* hidden state in and out [hidden] */
+    float* x_mid;  /* x' [hidden] */
+    float* qkv;    /* [n_q*hd + 2*n_kv*hd] */
+    float* attn;   /* [n_q*hd] */
+    float* h;      /* [inter] */
+} vkc_decode_buffers;
+size_t vkc_decode_program_bytes(const vkc_decode_dims* dims);
+int vkc_decode_program_build(const vkc_decode_dims* dims, const vkc_decode_layer* layers,
+                             const vkc_decode_buffers* bufs, const float* theta, void* program,
+                             size_t program_bytes, void* stream);
+int vkc_decode_program_run(const vkc_decode_dims* dims, void* program, int pos, void* stream);
 int vkc_attention_decode(const void* q, int q_bits, const void* kcache, const void* vcache,
                          float* out, int n_q, int n_kv, int head_dim, int ctx, float scale,
                          void* workspace, size_t workspace_bytes, void* stream);

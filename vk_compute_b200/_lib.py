@@ -72,6 +72,30 @@ class WeightEntry(C.Structure):
                 ("data", C.c_void_p), ("scale", C.c_void_p), ("zero", C.c_void_p)]
 
 
+class DecodeDims(C.Structure):
+    """vkc_decode_dims (include/vk_compute_b200.h)."""
+    _fields_ = [(n, C.c_int) for n in ("layers", "hidden", "inter", "n_q", "n_kv", "head_dim", "ctx_cap", "bits")] + [
+        ("eps", C.c_float)]
+
+
+class DecodeLayer(C.Structure):
+    """vkc_decode_layer (include/vk_compute_b200.h)."""
+    _fields_ = [(f"{m}{s}", C.c_void_p) for m in ("qkv", "o", "gate", "up", "down") for s in ("", "_scale", "_zero")] + [
+        ("gamma_attn", C.c_void_p), ("gamma_ffn", C.c_void_p), ("kcache", C.c_void_p), ("vcache", C.c_void_p)]
+
+
+class DecodeBuffers(C.Structure):
+    """vkc_decode_buffers (include/vk_compute_b200.h)."""
+    _fields_ = [(n, C.c_void_p) for n in ("x", "x_mid", "qkv", "attn", "h")]
+
+
+SIGNATURES.update({
+    "vkc_decode_program_bytes": (_sz, [C.POINTER(DecodeDims)]),
+    "vkc_decode_program_build": (_i, [C.POINTER(DecodeDims), C.POINTER(DecodeLayer), C.POINTER(DecodeBuffers), _p, _p,
+                                      _sz, _p]),
+    "vkc_decode_program_run": (_i, [C.POINTER(DecodeDims), _p, _i, _p]),
+})
+
 SIGNATURES.update({
     "vkc_weights_write": (_i, [C.c_char_p, C.POINTER(WeightEntry), _i]),
     "vkc_weights_open": (_i, [C.c_char_p, C.POINTER(C.c_void_p)]),

@@ -35,9 +35,11 @@
 // scalars applied in the epilogue, after the cluster reduction.
 #include "vkc_common.cuh"
 #include "vk_compute_b200.h"
+#include "attention_kernels.cuh"
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -229,7 +231,7 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
         out = out / (1.0f + exp2f(-out * 1.44269504f)) * v[1];
     }
     if constexpr (MODE == kGemv) {
-        if (p.residual && active && j < p.N) out += p.residual[j];
+        if (p.residual && active && j < p.N) out += __ldcg(p.residual + j);
     }
     if (active && j < p.N) {
         if (MODE == kGemv && p.peer_slots) {
@@ -615,15 +617,19 @@ __device__ __forceinline__ void sm_columns(int N, bool blocks, int cta, int ctas
     }
 }
 
-template <int BITS, int MODE, int kSmThreads, int D, bool IDP>
-__global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_sm_kernel(const GemvParams p) {
+// The body of the per-SM kernel for CTA `cta` of `ctas`, run by all
+// kSmThreads threads of the CTA with `smem` as its dynamic shared memory;
+// `wait()` stands for the wait on the previous kernel (called by all threads
+// after the weight ring is primed).
+template <int BITS, int MODE, int kSmThreads, int D, bool IDP, typename Wait>
+__device__ __forceinline__ void gemv_sm_body(const GemvParams& p, uint8_t* smem, const int cta, const int ctas,
+                                             Wait wait) {
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
     constexpr int KPC = 128 / BITS;
     constexpr bool kQuant = BITS <= 8;
     constexpr bool kNorm = MODE != kGemv;
     constexpr bool kIdp = IDP && kQuant;  // integer dot products (quantised weights)
 
-    extern __shared__ __align__(16) uint8_t smem[];
     uint4* ring = reinterpret_cast<uint4*>(smem);                                  // [NS][D][T]
     float* xs = reinterpret_cast<float*>(smem + NS * D * kSmThreads * 16);         // [R][NS][KPC] fp32 x'
     // integer-dot staging instead of xs: per chunk row and stream, the row's
@@ -639,7 +645,7 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
     int col0, C;
     // Reversed: the blocks split among one CTA more (the lighter CTAs) take
     // the highest CTA indices, which start last and measured slowest.
-    sm_columns(p.N, kQuant, gridDim.x - 1 - blockIdx.x, gridDim.x, col0, C);
+    sm_columns(p.N, kQuant, ctas - 1 - cta, ctas, col0, C);
     const int G = kSmThreads / C;
     const int c = tid % C, grp = tid / C;
     const bool streams = grp < G;  // the last threads (fewer than C) only stage activations
@@ -677,7 +683,8 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
     };
     auto load_x = [&](int j) {
         const int k = j * kPass + 4 * tid;
-        return k < nk ? *reinterpret_cast<const float4*>(p.x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        // L2 loads: x may come from other CTAs of a persistent kernel
+        return k < nk ? __ldcg(reinterpret_cast<const float4*>(p.x + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
     };
     float ss = 0.f, cz[NS];
 #pragma unroll
@@ -766,7 +773,7 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
     }
 
     // ---- x depends on the previous kernel: wait for it, then fold --------
-    pdl_wait();
+    wait();
 #pragma unroll
     for (int j = 0; j < kPre; ++j) xv[j] = j * kPass < nk ? load_x(j) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -862,6 +869,12 @@ __global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_s
         }
         finalize<MODE, NS, kQuant, kNorm>(p, col0 + tid, active, a, tot);
     }
+}
+
+template <int BITS, int MODE, int kSmThreads, int D, bool IDP>
+__global__ void __launch_bounds__(kSmThreads, kSmThreadsMax / kSmThreads) gemv_sm_kernel(const GemvParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    gemv_sm_body<BITS, MODE, kSmThreads, D, IDP>(p, smem, blockIdx.x, gridDim.x, [] { pdl_wait(); });
 }
 
 // ---- Batched decode: M activation vectors against one weight stream -------
@@ -1781,6 +1794,240 @@ int launch_batched_bits(int bits, const BatchParams& p, int M, bool norm, cudaSt
     return set_error(kErrArg, "unsupported weight width %d (expected 32, 16, 8 or 4)", bits);
 }
 
+
+// ---- Persistent decoder: every phase of every layer in one launch --------
+// One CTA of kPsThreads threads per SM runs, per layer, the five phases of a
+// decoder step -- the fused RMSNorm-QKV-RoPE projection with its KV-cache
+// append, attention, the O projection with the residual add, RMSNorm-SwiGLU,
+// the down projection with the residual add -- separated by grid-wide
+// barriers instead of kernel boundaries.  Each GEMV phase is the per-SM
+// kernel's body (all of K per CTA, balanced column ranges) and attention the
+// two-warp-group token-slice body, so the arithmetic is that of the separate
+// kernels.  A phase requests its weights (and attention the cache tiles of the
+// tokens before the newest) before it waits at the barrier, so the weight
+// stream of the next phase overlaps the end of the previous one on every SM.
+//
+// The barrier: an arrival counter in the program that only grows.  A CTA
+// arrives (all its threads' stores made visible first: __syncthreads, then one
+// fence and one atomic add by thread 0) once per phase; thread 0 waits until
+// the counter reaches base + phases-so-far * CTAs with acquire loads, bounded
+// by kGridWaitNs (on expiry it records kStatusGridTimeout and every later wait
+// of the launch gives up at once).  `base` is the counter at the start of the
+// launch, written by the previous launch's CTA 0 after its last barrier, so
+// graphs replay without resetting anything.  All CTAs must be resident: the
+// launch is cooperative.
+constexpr int kPsThreads = 384;  // 12 warps: registers for the attention phase without spills
+constexpr int kPsRing1 = 20;     // GEMV ring depth with one weight stream (120 KB per SM)
+constexpr int kPsRing2 = 10;     // with two (SwiGLU)
+constexpr int kPsAttnSync = 8;  // named barrier of the attention phase's warp groups (they use 1 and 2)
+constexpr uint32_t kStatusGridTimeout = 0x20u;
+constexpr uint64_t kGridWaitNs = kPeerWaitNs;
+
+struct DecodeLayer {
+    GemvParams qkv, o, ffn, down;
+    AttnParams att;
+};
+
+struct DecodeProgram {
+    unsigned count;  // barrier arrivals, growing across launches
+    unsigned base;   // the count at the start of the next launch
+    int layers;
+    int att_items;   // CTAs with an attention work item (n_kv * splits)
+    size_t smem;     // dynamic shared memory of the launch
+    int pad[2];
+};
+static_assert(sizeof(DecodeProgram) % 16 == 0, "layers follow the header");
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Thread 0's wait for the counter to reach `target` (the caller synchronises
+// its threads afterwards).
+__device__ __forceinline__ void grid_spin(const DecodeProgram* prog, unsigned target) {
+    const uint64_t deadline = globaltimer_ns() + kGridWaitNs;
+    uint32_t it = 0;
+    while (static_cast<int>(ld_acquire_gpu(&prog->count) - target) < 0) {
+        if ((++it & 63u) == 0) {
+            if (*reinterpret_cast<volatile uint32_t*>(&g_status) & kStatusGridTimeout) break;
+            if (globaltimer_ns() > deadline) {
+                atomicOr(&g_status, kStatusGridTimeout);
+                break;
+            }
+        }
+    }
+    __threadfence();
+}
+
+// Copies a parameter block from global to shared memory, one 4-byte word per
+// thread, all loads in flight at once (a field-by-field copy by one thread
+// would wait for each load in turn); the caller synchronises.
+template <typename T>
+__device__ __forceinline__ void stage_params(T* dst, const T* src) {
+    static_assert(sizeof(T) % 4 == 0, "whole words");
+    const unsigned* s = reinterpret_cast<const unsigned*>(src);
+    unsigned* d = reinterpret_cast<unsigned*>(dst);
+    for (int i = threadIdx.x; i < static_cast<int>(sizeof(T) / 4); i += blockDim.x) d[i] = __ldcg(s + i);
+}
+
+template <int BITS, int G, int HD>
+__global__ void __launch_bounds__(kPsThreads, 1) decode_program_kernel(DecodeProgram* prog, int pos) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ GemvParams sg;
+    __shared__ AttnParams sa;
+    __shared__ unsigned s_base;
+    constexpr int kAttThreadsPs = 2 * kFaThreads;  // two warp groups
+    const int tid = threadIdx.x, cta = blockIdx.x, ctas = gridDim.x;
+    if (tid == 0) s_base = *reinterpret_cast<volatile unsigned*>(&prog->base);
+    __syncthreads();
+    const unsigned base = s_base;
+    const DecodeLayer* layers = reinterpret_cast<const DecodeLayer*>(prog + 1);
+    const int L = prog->layers, att_items = prog->att_items;
+    unsigned k = 0;  // barriers of this launch passed so far
+    auto arrive = [&] {
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(&prog->count, 1u);
+        }
+        ++k;
+    };
+    auto wait_all = [&] {
+        if (tid == 0) grid_spin(prog, base + k * static_cast<unsigned>(ctas));
+        __syncthreads();
+    };
+    auto wait_att = [&] {
+        if (tid == 0) grid_spin(prog, base + k * static_cast<unsigned>(ctas));
+        part_sync<kPsAttnSync, kAttThreadsPs>();
+    };
+    auto gemv_phase = [&](const GemvParams& src, auto mode_tag, auto ring_tag) {
+        constexpr int MODE = decltype(mode_tag)::value, D = decltype(ring_tag)::value;
+        stage_params(&sg, &src);
+        __syncthreads();
+        if (tid == 0) sg.pos = pos;
+        __syncthreads();
+        gemv_sm_body<BITS, MODE, kPsThreads, D, true>(sg, smem, cta, ctas, wait_all);
+        arrive();
+    };
+    using One = std::integral_constant<int, kPsRing1>;
+    using Two = std::integral_constant<int, kPsRing2>;
+    for (int l = 0; l < L; ++l) {
+        const DecodeLayer& e = layers[l];
+        gemv_phase(e.qkv, std::integral_constant<int, kRopePairs>(), One());
+        // attention over tokens [0, pos]: the tiles of tokens before pos are
+        // requested before the barrier (only this layer's QKV phase writes pos)
+        stage_params(&sa, &e.att);
+        __syncthreads();
+        if (tid == 0) {
+            sa.ctx = pos + 1;
+            sa.stable = pos;
+        }
+        __syncthreads();
+        if (cta < att_items) {
+            if (tid < kAttThreadsPs)
+                attention_fa_body<G, HD, kFaDeepStages, 1, 2, kPsAttnSync>(sa, smem, cta % sa.splits, cta / sa.splits,
+                                                                            wait_att);
+        } else if (tid == 0) {
+            grid_spin(prog, base + k * static_cast<unsigned>(ctas));
+        }
+        arrive();
+        gemv_phase(e.o, std::integral_constant<int, kGemv>(), One());
+        gemv_phase(e.ffn, std::integral_constant<int, kSwiglu>(), Two());
+        gemv_phase(e.down, std::integral_constant<int, kGemv>(), One());
+    }
+    if (cta == 0 && tid == 0) {
+        // every CTA has arrived k times: the next launch starts from here
+        grid_spin(prog, base + k * static_cast<unsigned>(ctas));
+        *reinterpret_cast<volatile unsigned*>(&prog->base) = base + k * static_cast<unsigned>(ctas);
+        __threadfence();
+    }
+}
+
+// Host side of the persistent decoder.
+size_t decode_program_header_bytes(int layers) {
+    const size_t b = sizeof(DecodeProgram) + static_cast<size_t>(layers) * sizeof(DecodeLayer);
+    return (b + 255) & ~static_cast<size_t>(255);
+}
+
+size_t decode_gemv_smem(int NS, int K) { return sm_smem_bytes(NS, kPsThreads, NS == 1 ? kPsRing1 : kPsRing2, K); }
+
+// Whether one GEMV phase of the persistent decoder can run the per-SM body:
+// the conditions of sm_kernel_fits for kPsThreads threads.
+bool decode_gemv_fits(int N, int K, int sms, bool quant) {
+    if (N % 2 != 0) return false;
+    if (quant) {
+        const int nb = N / kGroup;
+        if (N % kGroup != 0 || nb > sms || (sms + nb - 1) / nb > kGroup / 2) return false;
+        // columns per CTA (at most 256 / floor(sms / nb)) leave every thread a row group
+        const int per = sms / nb;
+        if ((kGroup + per - 1) / per > kPsThreads) return false;
+    } else if (N / 2 < sms || N / sms > kPsThreads - 2) {
+        return false;
+    }
+    return K > 0;
+}
+
+// Per-SM attention split of the persistent decoder for a cache of ctx_cap
+// tokens over `ctas` CTAs (the standalone per-SM plan, sized for the whole
+// cache: CTAs whose range lies past the current context have no tokens).
+void decode_attention_split(int n_kv, int hd, int ctx_cap, int ctas, int* splits, int* tpc) {
+    const int tt = 8192 / hd;
+    const int per_head = ctas / n_kv > 0 ? ctas / n_kv : 1;
+    int t = (ctx_cap + per_head - 1) / per_head;
+    t = ((t + 15) / 16) * 16;
+    if (t < 2 * tt) t = 2 * tt;
+    *tpc = t;
+    *splits = (ctx_cap + t - 1) / t;
+}
+
+size_t decode_attention_ws_bytes(const vkc_decode_dims& d, int ctas) {
+    int splits = 0, tpc = 0;
+    decode_attention_split(d.n_kv, d.head_dim, d.ctx_cap, ctas, &splits, &tpc);
+    return 256 + static_cast<size_t>(d.n_q) * splits * (d.head_dim + 4) * sizeof(float);
+}
+
+size_t decode_attention_smem(int hd) {
+    return hd == 64 ? static_cast<size_t>(kFaDeepStages) * MmaGeo<64>::SU * 16 + MmaGeo<64>::q_bytes
+                    : static_cast<size_t>(kFaDeepStages) * MmaGeo<128>::SU * 16 + MmaGeo<128>::q_bytes;
+}
+
+size_t decode_program_smem(const vkc_decode_dims& d) {
+    size_t s = decode_attention_smem(d.head_dim);
+    const int q_rows = d.n_q * d.head_dim;
+    s = std::max(s, decode_gemv_smem(1, d.hidden));  // QKV
+    s = std::max(s, decode_gemv_smem(1, q_rows));    // O
+    s = std::max(s, decode_gemv_smem(2, d.hidden));  // gate/up
+    s = std::max(s, decode_gemv_smem(1, d.inter));   // down
+    return s;
+}
+
+int decode_check_dims(const vkc_decode_dims* d, int sms) {
+    if (!d) return set_error(kErrArg, "null decoder dimensions");
+    if (d->layers <= 0) return set_error(kErrArg, "layers=%d must be positive", d->layers);
+    if (d->bits != 4) return set_error(kErrUnsupported, "the persistent decoder runs 4-bit weights (bits=%d)", d->bits);
+    if (d->head_dim != 128 && d->head_dim != 64)
+        return set_error(kErrUnsupported, "persistent decoder: head_dim %d (64 or 128)", d->head_dim);
+    if (d->n_kv <= 0 || d->n_q != 4 * d->n_kv)
+        return set_error(kErrUnsupported, "persistent decoder: 4 query heads per KV head (n_q=%d n_kv=%d)", d->n_q,
+                         d->n_kv);
+    if (d->ctx_cap <= 0) return set_error(kErrArg, "ctx_cap=%d must be positive", d->ctx_cap);
+    const int q_rows = d->n_q * d->head_dim, kv_rows = d->n_kv * d->head_dim;
+    const int kpc = 128 / d->bits;
+    if (d->hidden % kpc || q_rows % kpc || d->inter % kpc)
+        return set_error(kErrArg, "hidden, heads*head_dim and inter must be multiples of %d", kpc);
+    if (!decode_gemv_fits(q_rows + 2 * kv_rows, d->hidden, sms, true) || !decode_gemv_fits(d->hidden, q_rows, sms, true) ||
+        !decode_gemv_fits(d->inter, d->hidden, sms, true) || !decode_gemv_fits(d->hidden, d->inter, sms, true))
+        return set_error(kErrUnsupported, "persistent decoder: a projection does not split over %d SMs", sms);
+    int splits = 0, tpc = 0;
+    decode_attention_split(d->n_kv, d->head_dim, d->ctx_cap, sms, &splits, &tpc);
+    if (d->n_kv * splits > sms) return set_error(kErrUnsupported, "persistent decoder: attention needs more CTAs than SMs");
+    if (decode_program_smem(*d) + 1024 > 227u * 1024)
+        return set_error(kErrUnsupported, "persistent decoder: shared memory exceeds an SM's");
+    return kOk;
+}
+
 int check_common(int bits, int N, int K, const void* w, const float* s, const float* z, const float* x,
                  const float* y, const float* gamma) {
     if (bits != 32 && bits != 16 && bits != 8 && bits != 4)
@@ -2055,6 +2302,158 @@ int vkc_rmsnorm_gemv_batched(int bits, const void* w, const float* scale, const 
 
 // Status word of the current device (bits: kStatus*).  Reading waits for the
 // device; `clear` resets it.
+
+size_t vkc_decode_program_bytes(const vkc_decode_dims* dims) {
+    int sms = 0;
+    if (!dims || sm_count(&sms) != kOk) return 0;
+    return decode_program_header_bytes(dims->layers) + decode_attention_ws_bytes(*dims, sms);
+}
+
+int vkc_decode_program_build(const vkc_decode_dims* dims, const vkc_decode_layer* layers,
+                             const vkc_decode_buffers* bufs, const float* theta, void* program, size_t program_bytes,
+                             void* stream) {
+    int sms = 0;
+    if (int e = sm_count(&sms)) return e;
+    if (int e = decode_check_dims(dims, sms)) return e;
+    const vkc_decode_dims& d = *dims;
+    if (!layers || !bufs || !theta || !program) return set_error(kErrArg, "null decoder argument");
+    if (!bufs->x || !bufs->x_mid || !bufs->qkv || !bufs->attn || !bufs->h) return set_error(kErrArg, "null decoder buffer");
+    if (reinterpret_cast<uintptr_t>(program) % 256 != 0) return set_error(kErrArg, "program must be 256-byte aligned");
+    const size_t need = vkc_decode_program_bytes(dims);
+    if (program_bytes < need) return set_error(kErrArg, "decoder program holds %zu bytes, needs %zu", program_bytes, need);
+    const int hd = d.head_dim, q_rows = d.n_q * hd, kv_rows = d.n_kv * hd, nqkv = q_rows + 2 * kv_rows;
+    const int kpc = 128 / d.bits;
+    const size_t hbytes = decode_program_header_bytes(d.layers);
+    char* ws = static_cast<char*>(program) + hbytes;
+    int splits = 0, tpc = 0;
+    decode_attention_split(d.n_kv, hd, d.ctx_cap, sms, &splits, &tpc);
+    std::vector<char> host(hbytes, 0);
+    DecodeProgram* prog = reinterpret_cast<DecodeProgram*>(host.data());
+    prog->layers = d.layers;
+    prog->att_items = d.n_kv * splits;
+    prog->smem = decode_program_smem(d);
+    DecodeLayer* out = reinterpret_cast<DecodeLayer*>(prog + 1);
+    auto base_params = [&](const void* w, const float* s, const float* z, int N, int K) {
+        GemvParams p = {};
+        p.w[0] = static_cast<const uint8_t*>(w);
+        p.s[0] = s;
+        p.z[0] = z;
+        p.N = N;
+        p.K = K;
+        p.R = K / kpc;
+        return p;
+    };
+    for (int l = 0; l < d.layers; ++l) {
+        const vkc_decode_layer& w = layers[l];
+        if (int e = check_common(d.bits, nqkv, d.hidden, w.qkv, w.qkv_scale, w.qkv_zero, bufs->x, bufs->qkv,
+                                 w.gamma_attn))
+            return e;
+        if (int e = check_common(d.bits, d.hidden, q_rows, w.o, w.o_scale, w.o_zero, bufs->attn, bufs->x_mid, nullptr))
+            return e;
+        if (int e = check_common(d.bits, d.inter, d.hidden, w.gate, w.gate_scale, w.gate_zero, bufs->x_mid, bufs->h,
+                                 w.gamma_ffn))
+            return e;
+        if (int e = check_common(d.bits, d.inter, d.hidden, w.up, w.up_scale, w.up_zero, bufs->x_mid, bufs->h,
+                                 w.gamma_ffn))
+            return e;
+        if (int e = check_common(d.bits, d.hidden, d.inter, w.down, w.down_scale, w.down_zero, bufs->h, bufs->x, nullptr))
+            return e;
+        if (!w.gamma_attn || !w.gamma_ffn || !w.kcache || !w.vcache) return set_error(kErrArg, "null layer %d field", l);
+        if ((reinterpret_cast<uintptr_t>(w.kcache) | reinterpret_cast<uintptr_t>(w.vcache)) % 16 != 0)
+            return set_error(kErrArg, "layer %d: caches must be 16-byte aligned", l);
+        DecodeLayer& L = out[l];
+        // RMSNorm-QKV-RoPE with the KV append, rows [Q | K0 V0 | K1 V1 | ...]
+        L.qkv = base_params(w.qkv, w.qkv_scale, w.qkv_zero, nqkv, d.hidden);
+        L.qkv.x = bufs->x;
+        L.qkv.gamma = w.gamma_attn;
+        L.qkv.theta = theta;
+        L.qkv.y = bufs->qkv;
+        L.qkv.eps = d.eps;
+        L.qkv.inv_dim = 1.0f / static_cast<float>(d.hidden);
+        L.qkv.head_dim = hd;
+        L.qkv.rot_rows = q_rows + kv_rows;
+        L.qkv.kcache = static_cast<uint16_t*>(w.kcache);
+        L.qkv.vcache = static_cast<uint16_t*>(w.vcache);
+        L.qkv.q_rows = q_rows;
+        L.qkv.kv_rows = kv_rows;
+        L.qkv.kv_interleave = 1;
+        L.qkv.ctx_cap = d.ctx_cap;
+        // attention over the layer's cache
+        AttnParams& a = L.att;
+        a.q = bufs->qkv;
+        a.q_bits = 32;
+        a.kc = static_cast<const uint4*>(w.kcache);
+        a.vc = static_cast<const uint4*>(w.vcache);
+        a.out = bufs->attn;
+        a.tickets = reinterpret_cast<unsigned*>(ws);
+        a.ws = reinterpret_cast<float*>(ws + 256);
+        a.n_q = d.n_q;
+        a.n_kv = d.n_kv;
+        a.hd = hd;
+        a.ctx = d.ctx_cap;
+        a.splits = splits;
+        a.tpc = tpc;
+        a.ctx_cap = d.ctx_cap;
+        a.tt = 8192 / hd;
+        a.scale_log2 = kLog2e / sqrtf(static_cast<float>(hd));
+        a.pitch = hd + 4;
+        a.smem = static_cast<int>(prog->smem);
+        // O projection + residual: x' = x + O attn
+        L.o = base_params(w.o, w.o_scale, w.o_zero, d.hidden, q_rows);
+        L.o.x = bufs->attn;
+        L.o.residual = bufs->x;
+        L.o.y = bufs->x_mid;
+        // RMSNorm-SwiGLU: h = silu(gate x'') * up x''
+        L.ffn = base_params(w.gate, w.gate_scale, w.gate_zero, d.inter, d.hidden);
+        L.ffn.w[1] = static_cast<const uint8_t*>(w.up);
+        L.ffn.s[1] = w.up_scale;
+        L.ffn.z[1] = w.up_zero;
+        L.ffn.x = bufs->x_mid;
+        L.ffn.gamma = w.gamma_ffn;
+        L.ffn.y = bufs->h;
+        L.ffn.eps = d.eps;
+        L.ffn.inv_dim = 1.0f / static_cast<float>(d.hidden);
+        // down projection + residual: x = x' + down h
+        L.down = base_params(w.down, w.down_scale, w.down_zero, d.hidden, d.inter);
+        L.down.x = bufs->h;
+        L.down.residual = bufs->x_mid;
+        L.down.y = bufs->x;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    VKC_CUDA_TRY(cudaMemcpyAsync(program, host.data(), hbytes, cudaMemcpyHostToDevice, s));
+    VKC_CUDA_TRY(cudaMemsetAsync(ws, 0, 256, s));  // attention tickets
+    VKC_CUDA_TRY(cudaStreamSynchronize(s));        // the host copy goes out of scope
+    return kOk;
+}
+
+int vkc_decode_program_run(const vkc_decode_dims* dims, void* program, int pos, void* stream) {
+    int sms = 0;
+    if (int e = sm_count(&sms)) return e;
+    if (int e = decode_check_dims(dims, sms)) return e;
+    if (!program) return set_error(kErrArg, "null decoder program");
+    if (pos < 0 || pos >= dims->ctx_cap) return set_error(kErrArg, "pos=%d outside the cache of %d tokens", pos, dims->ctx_cap);
+    const size_t smem = decode_program_smem(*dims);
+    const void* kern = dims->head_dim == 128 ? reinterpret_cast<const void*>(decode_program_kernel<4, 4, 128>)
+                                             : reinterpret_cast<const void*>(decode_program_kernel<4, 4, 64>);
+    if (int e = ensure_smem(kern, smem)) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms, 1, 1);
+    cfg.blockDim = dim3(kPsThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeCooperative;  // every CTA resident: the phases wait on one another
+    attr.val.cooperative = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    DecodeProgram* prog = static_cast<DecodeProgram*>(program);
+    if (dims->head_dim == 128)
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_program_kernel<4, 4, 128>, prog, pos));
+    else
+        VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_program_kernel<4, 4, 64>, prog, pos));
+    return kOk;
+}
+
 int vkc_set_gemv_plan(int plan) {
     if (plan < 0 || plan > 4) return set_error(kErrArg, "GEMV plan %d (expected 0 to 4)", plan);
     g_gemv_plan = plan;

@@ -263,7 +263,9 @@ class ShardedDecoder:
     dependent launch each kernel becomes resident beside its predecessor and
     streams its first weights or cache tiles while that one finishes; "mixed"
     runs the GEMVs in half an SM (four consecutive GEMVs per layer overlap
-    pairwise) and attention through the 6-stage ring.
+    pairwise) and attention through the 6-stage ring; "persistent" runs the
+    whole step as one cooperative kernel (one GPU, 4-bit weights), its phases
+    separated by grid barriers (vkc_decode_program_run).
     """
 
     EXCHANGES = ("p2p", "p2p-kernel", "nccl", "none")
@@ -271,7 +273,7 @@ class ShardedDecoder:
     # CTA resident beside a clustered attention kernel would leave room for
     # only one of its two CTAs per SM and split its grid into two waves.
     SHAPES = {"full": ("auto-full", None), "half": ("per-sm-half", "per-sm-half"),
-              "mixed": ("per-sm-half", "per-sm")}
+              "mixed": ("per-sm-half", "per-sm"), "persistent": ("auto-full", None)}
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, device=None, seed: int = 0,
                  group=None, layers: list[LayerShard] | None = None, exchange: str = "p2p", shape: str = "full"):
@@ -297,6 +299,11 @@ class ShardedDecoder:
             x=z(H), x_mid=z(H), qkv=z(len(p.qkv_cols)), attn=z(p.n_q * hd),
             h=z(p.ffn_rows[1] - p.ffn_rows[0]), o_part=z(H), d_part=z(H),
             ws=self._with_plans(lambda: ops.attention_workspace(p.n_q, p.n_kv, hd, cfg.ctx, device=self.device)))
+        self.program = None
+        if shape == "persistent":
+            if p.world != 1 and self.exchange != "none":
+                raise ValueError("the persistent decoder step runs on one GPU")
+            self._build_program()
         if self.exchange in ("p2p", "p2p-kernel"):
             from .p2p import PeerGather
 
@@ -335,6 +342,49 @@ class ShardedDecoder:
             self.peer.close()
             self.peer = None
 
+    def _build_program(self) -> None:
+        """The step as one persistent kernel (vkc_decode_program_build)."""
+        import ctypes as C
+
+        from ._lib import DecodeBuffers, DecodeDims, DecodeLayer, check, lib
+
+        cfg, p, b = self.cfg, self.plan, self.buf
+        self._dims = DecodeDims(layers=len(self.layers), hidden=cfg.hidden, inter=p.ffn_rows[1] - p.ffn_rows[0],
+                                n_q=p.n_q, n_kv=p.n_kv, head_dim=cfg.head_dim, ctx_cap=cfg.ctx, bits=cfg.bits,
+                                eps=cfg.eps)
+        if self.layers[0].o.K != p.n_q * cfg.head_dim:
+            raise ValueError("the O projection's input is not this rank's heads")
+        arr = (DecodeLayer * len(self.layers))()
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        for i, L in enumerate(self.layers):
+            e = arr[i]
+            for name, w in (("qkv", L.qkv), ("o", L.o), ("gate", L.gate), ("up", L.up), ("down", L.down)):
+                setattr(e, name, ptr(w.packed))
+                setattr(e, name + "_scale", ptr(w.scale))
+                setattr(e, name + "_zero", ptr(w.zero))
+            e.gamma_attn, e.gamma_ffn = L.g_attn.data_ptr(), L.g_ffn.data_ptr()
+            e.kcache, e.vcache = L.kcache.data_ptr(), L.vcache.data_ptr()
+        bufs = DecodeBuffers(x=b.x.data_ptr(), x_mid=b.x_mid.data_ptr(), qkv=b.qkv.data_ptr(), attn=b.attn.data_ptr(),
+                             h=b.h.data_ptr())
+        nbytes = lib().vkc_decode_program_bytes(C.byref(self._dims))
+        if nbytes == 0:
+            raise RuntimeError("vkc_decode_program_bytes failed")
+        self.program = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().vkc_decode_program_build(C.byref(self._dims), arr, C.byref(bufs), self.theta.data_ptr(),
+                                             self.program.data_ptr(), nbytes, st))
+
+    def _run_program(self, pos: int) -> torch.Tensor:
+        import ctypes as C
+
+        from ._lib import check, lib
+
+        if not 0 <= pos < self.cfg.ctx:
+            raise ValueError(f"position {pos} outside the cache of {self.cfg.ctx} tokens")
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().vkc_decode_program_run(C.byref(self._dims), self.program.data_ptr(), pos, st))
+        return self.buf.x
+
     def _with_plans(self, fn):
         """fn() under this decoder's GEMV and attention plans (per host
         thread), restoring the caller's afterwards."""
@@ -349,6 +399,8 @@ class ShardedDecoder:
             ops.set_attention_plan(prev_a)
 
     def step(self, pos: int) -> torch.Tensor:
+        if self.program is not None:
+            return self._run_program(pos)
         return self._with_plans(lambda: self._step(pos))
 
     def _step(self, pos: int) -> torch.Tensor:
@@ -397,6 +449,8 @@ class ShardedDecoder:
 
     def kernels_per_step(self) -> int:
         """Launches of this library per step (collective-library kernels excluded)."""
+        if self.program is not None:
+            return 1
         if self.exchange == "p2p":
             return 5 * self.cfg.layers + 1
         return (7 if self.exchange == "p2p-kernel" else 5) * self.cfg.layers

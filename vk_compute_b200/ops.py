@@ -455,7 +455,8 @@ def get_gemv_plan() -> str:
 
 def device_status(clear: bool = False) -> int:
     """Status word of the current device (waits for it); flags 0x1 producer,
-    0x2 consumer, 0x4 cluster reduction, 0x8 peer-exchange wait ran out."""
+    0x2 consumer, 0x4 cluster reduction, 0x8 peer-exchange, 0x10 tcgen05
+    GEMM pipeline, 0x20 persistent-decoder grid barrier wait ran out."""
     v = C.c_uint(0)
     check(lib().vkc_device_status(C.byref(v), int(clear)))
     return int(v.value)
