@@ -56,6 +56,7 @@ struct AttnParams {
     int pitch;          // floats per partial record, hd + 4 (a multiple of 4)
     int smem;           // dynamic shared memory of the launch (bytes)
     int stable;         // tokens [0, stable) are written by no kernel still in flight
+    int pre_max;        // sub-tiles per warp group requested before the wait (0: as many as stable allows)
 };
 
 namespace {
@@ -283,28 +284,34 @@ __device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv,
     part_sync<SYNC, NT>();
     if (s_ticket != static_cast<unsigned>(S - 1)) return;
     __threadfence();
-    if (tid < G * HD / 4) {
-        const int g = (4 * tid) / HD, d = 4 * tid - g * HD;
-        const int h = kv * G + g;
+    // TPU threads per float4 unit (lanes next to each other), each folding
+    // the splits s = part, part + TPU, ... in order; the parts combine in
+    // part order through lane shuffles.
+    constexpr int kUnits = G * HD / 4;
+    constexpr int TPU = NT >= 2 * kUnits ? 2 : 1;
+    const int unit = tid / TPU, part = tid % TPU;
+    float M = -INFINITY, L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int g = (4 * unit) / HD, d = 4 * unit - g * HD;
+    const int h = kv * G + g;
+    if (unit < kUnits) {
         const float* rec = p.ws + static_cast<size_t>(h) * S * p.pitch;
-        float M = -INFINITY, L = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        // (a body sharing its kernel's registers with other phases, SYNC != 0,
-        // takes 8 records per round trip)
-        constexpr int kChunk = SYNC == 0 ? 24 : 8;
-        for (int s0 = 0; s0 < S; s0 += kChunk) {
+        // records per round trip (fewer in a body sharing its kernel's
+        // registers with other phases, SYNC != 0)
+        constexpr int kChunk = SYNC == 0 ? 24 / TPU : 12 / TPU;
+        for (int s0 = part; s0 < S; s0 += kChunk * TPU) {
             float2 ml[kChunk];
             float4 v[kChunk];
 #pragma unroll
             for (int i = 0; i < kChunk; ++i) {
-                const float* r = rec + static_cast<size_t>(min(s0 + i, S - 1)) * p.pitch;
+                const float* r = rec + static_cast<size_t>(min(s0 + i * TPU, S - 1)) * p.pitch;
                 ml[i] = __ldcg(reinterpret_cast<const float2*>(r + HD));
                 v[i] = __ldcg(reinterpret_cast<const float4*>(r + d));
             }
             float Mc = M;
 #pragma unroll
             for (int i = 0; i < kChunk; ++i)
-                if (s0 + i < S) Mc = fmaxf(Mc, ml[i].x);
+                if (s0 + i * TPU < S) Mc = fmaxf(Mc, ml[i].x);
             if (Mc == -INFINITY) continue;
             const float f = M == -INFINITY ? 0.f : exp2f(M - Mc);
             acc.x *= f;
@@ -315,7 +322,7 @@ __device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv,
             M = Mc;
 #pragma unroll
             for (int i = 0; i < kChunk; ++i) {
-                if (s0 + i >= S || ml[i].x == -INFINITY) continue;
+                if (s0 + i * TPU >= S || ml[i].x == -INFINITY) continue;
                 const float w = exp2f(ml[i].x - M);
                 L = fmaf(w, ml[i].y, L);
                 acc.x = fmaf(w, v[i].x, acc.x);
@@ -324,6 +331,24 @@ __device__ __forceinline__ void merge_splits_direct(const AttnParams& p, int kv,
                 acc.w = fmaf(w, v[i].w, acc.w);
             }
         }
+    }
+    if constexpr (TPU == 2) {
+        // part 0 takes part 1's state (the lane above it)
+        const float M1 = __shfl_down_sync(0xffffffffu, M, 1), L1 = __shfl_down_sync(0xffffffffu, L, 1);
+        float4 a1;
+        a1.x = __shfl_down_sync(0xffffffffu, acc.x, 1);
+        a1.y = __shfl_down_sync(0xffffffffu, acc.y, 1);
+        a1.z = __shfl_down_sync(0xffffffffu, acc.z, 1);
+        a1.w = __shfl_down_sync(0xffffffffu, acc.w, 1);
+        const float Mt = fmaxf(M, M1);
+        const float f0 = M == -INFINITY ? 0.f : exp2f(M - Mt), f1 = M1 == -INFINITY ? 0.f : exp2f(M1 - Mt);
+        L = L * f0 + L1 * f1;
+        acc.x = acc.x * f0 + a1.x * f1;
+        acc.y = acc.y * f0 + a1.y * f1;
+        acc.z = acc.z * f0 + a1.z * f1;
+        acc.w = acc.w * f0 + a1.w * f1;
+    }
+    if (unit < kUnits && part == 0) {
         const float inv = 1.f / L;
         *reinterpret_cast<float4*>(p.out + static_cast<size_t>(h) * HD + d) =
             make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
@@ -942,7 +967,9 @@ __device__ __forceinline__ void attention_fa_body(const AttnParams& p, uint8_t* 
     // in flight writes) are requested before the wait on the previous kernel;
     // the rest, and q, after it.  Commit groups stay in sub-tile order.
     int s_pre = wg;
-    while (s_pre < ST && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable) {
+    for (int n = 0; s_pre < ST && s_pre < nsub && t0 + min(T, (s_pre + 1) * TT) <= p.stable &&
+                    (p.pre_max == 0 || n < p.pre_max);
+         ++n) {
         issue(s_pre);
         cp_commit();
         s_pre += NWG;

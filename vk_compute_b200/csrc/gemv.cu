@@ -621,9 +621,13 @@ __device__ __forceinline__ void sm_columns(int N, bool blocks, int cta, int ctas
 // kSmThreads threads of the CTA with `smem` as its dynamic shared memory;
 // `wait()` stands for the wait on the previous kernel (called by all threads
 // after the weight ring is primed).
-template <int BITS, int MODE, int kSmThreads, int D, bool IDP, typename Wait>
+// UNROLL false: a compact stream loop; PRIME: ring rows requested before the
+// wait (the rest right after it), fewer where the wait itself goes through
+// this SM's memory pipeline.
+template <int BITS, int MODE, int kSmThreads, int D, bool IDP, bool UNROLL = true, int PRIME = D, typename Wait>
 __device__ __forceinline__ void gemv_sm_body(const GemvParams& p, uint8_t* smem, const int cta, const int ctas,
                                              Wait wait) {
+    static_assert(PRIME >= 1 && PRIME <= D, "prime rows");
     constexpr int NS = MODE == kSwiglu ? 2 : 1;
     constexpr int KPC = 128 / BITS;
     constexpr bool kQuant = BITS <= 8;
@@ -760,8 +764,7 @@ __device__ __forceinline__ void gemv_sm_body(const GemvParams& p, uint8_t* smem,
     for (int st = 0; st < NS; ++st)
         wp[st] = reinterpret_cast<const uint4*>(p.w[st]) + (static_cast<size_t>(grp) * p.N + col);
     const uint32_t slot0 = smem_addr(ring + tid);
-#pragma unroll
-    for (int u = 0; u < D; ++u) {
+    auto prime = [&](int u) {
         if (u < my_rows) {
 #pragma unroll
             for (int st = 0; st < NS; ++st) {
@@ -770,19 +773,38 @@ __device__ __forceinline__ void gemv_sm_body(const GemvParams& p, uint8_t* smem,
             }
         }
         cp_async_commit();
-    }
+    };
+#pragma unroll
+    for (int u = 0; u < PRIME; ++u) prime(u);
 
     // ---- x depends on the previous kernel: wait for it, then fold --------
     wait();
+#pragma unroll
+    for (int u = PRIME; u < D; ++u) prime(u);
 #pragma unroll
     for (int j = 0; j < kPre; ++j) xv[j] = j * kPass < nk ? load_x(j) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < kPre; ++j)
         if (j * kPass < nk) fold(j, xv[j], gs[j], gz[j]);
-    for (int j = kPre; j * kPass < nk; ++j) {
-        float4 g_s[NS], g_z[NS];
-        load_acts(j, g_s, g_z);
-        fold(j, load_x(j), g_s, g_z);
+    if (kPre * kPass < nk) {
+        // later passes: the next pass's loads are in flight while this one folds
+        float4 n_s[NS], n_z[NS], nx;
+        load_acts(kPre, n_s, n_z);
+        nx = load_x(kPre);
+        for (int j = kPre; j * kPass < nk; ++j) {
+            float4 g_s[NS], g_z[NS];
+#pragma unroll
+            for (int st = 0; st < NS; ++st) {
+                g_s[st] = n_s[st];
+                g_z[st] = n_z[st];
+            }
+            const float4 x4 = nx;
+            if ((j + 1) * kPass < nk) {
+                load_acts(j + 1, n_s, n_z);
+                nx = load_x(j + 1);
+            }
+            fold(j, x4, g_s, g_z);
+        }
     }
     __syncthreads();
 
@@ -799,7 +821,37 @@ __device__ __forceinline__ void gemv_sm_body(const GemvParams& p, uint8_t* smem,
     const float* xrow = xs + grp * NS * KPC;
     const int xstep = G * NS * KPC;
     int xr = grp;  // chunk row (integer-dot staging)
-    for (int i = 0; i < my_rows; i += D) {
+    if constexpr (!UNROLL) {
+        // one row per iteration, the ring slot a running index: compact code
+        // for a kernel that holds several phases
+        int u = 0;
+#pragma unroll 1
+        for (int i = 0; i < my_rows; ++i) {
+            cp_async_wait<D - 1>();
+#pragma unroll
+            for (int st = 0; st < NS; ++st) {
+                const uint4 chunk = ring[(st * D + u) * kSmThreads + tid];
+                if constexpr (kIdp) {
+                    const int off = (xr * NS + st) * KPC;
+                    accf[st] = fmaf(xsig[xr * NS + st], chunk_idot<BITS>(chunk, xh + off, xl + off), accf[st]);
+                } else {
+                    chunk_fma<BITS>(chunk, xrow + st * KPC, acc[st]);
+                }
+            }
+            xrow += xstep;
+            xr += G;
+            if (i + D < my_rows) {
+#pragma unroll
+                for (int st = 0; st < NS; ++st) {
+                    cp_async16(slot0 + static_cast<uint32_t>((st * D + u) * kSmThreads * 16), wp[st]);
+                    wp[st] += row_step;
+                }
+            }
+            cp_async_commit();
+            u = u + 1 == D ? 0 : u + 1;
+        }
+    }
+    for (int i = 0; UNROLL && i < my_rows; i += D) {
 #pragma unroll
         for (int u = 0; u < D; ++u) {
             if (i + u < my_rows) {
@@ -1819,6 +1871,13 @@ int launch_batched_bits(int bits, const BatchParams& p, int M, bool norm, cudaSt
 constexpr int kPsThreads = 384;  // 12 warps: registers for the attention phase without spills
 constexpr int kPsRing1 = 20;     // GEMV ring depth with one weight stream (120 KB per SM)
 constexpr int kPsRing2 = 10;     // with two (SwiGLU)
+// Ring rows (and attention sub-tiles per warp group) requested before a
+// barrier wait: the wait's polls and the __syncthreads after it queue behind
+// this SM's outstanding requests, so a phase primes only what bridges the
+// barrier and requests the rest once it has passed.
+constexpr int kPsPrime1 = 4;
+constexpr int kPsPrime2 = 2;
+constexpr int kPsAttnPrime = 1;
 constexpr int kPsAttnSync = 8;  // named barrier of the attention phase's warp groups (they use 1 and 2)
 constexpr uint32_t kStatusGridTimeout = 0x20u;
 constexpr uint64_t kGridWaitNs = kPeerWaitNs;
@@ -1838,9 +1897,9 @@ struct DecodeProgram {
 };
 static_assert(sizeof(DecodeProgram) % 16 == 0, "layers follow the header");
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
     unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -1849,7 +1908,8 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 __device__ __forceinline__ void grid_spin(const DecodeProgram* prog, unsigned target) {
     const uint64_t deadline = globaltimer_ns() + kGridWaitNs;
     uint32_t it = 0;
-    while (static_cast<int>(ld_acquire_gpu(&prog->count) - target) < 0) {
+    // relaxed polls; the fence below orders the phase's reads after them
+    while (static_cast<int>(ld_relaxed_gpu(&prog->count) - target) < 0) {
         if ((++it & 63u) == 0) {
             if (*reinterpret_cast<volatile uint32_t*>(&g_status) & kStatusGridTimeout) break;
             if (globaltimer_ns() > deadline) {
@@ -1858,33 +1918,28 @@ __device__ __forceinline__ void grid_spin(const DecodeProgram* prog, unsigned ta
             }
         }
     }
-    __threadfence();
-}
-
-// Copies a parameter block from global to shared memory, one 4-byte word per
-// thread, all loads in flight at once (a field-by-field copy by one thread
-// would wait for each load in turn); the caller synchronises.
-template <typename T>
-__device__ __forceinline__ void stage_params(T* dst, const T* src) {
-    static_assert(sizeof(T) % 4 == 0, "whole words");
-    const unsigned* s = reinterpret_cast<const unsigned*>(src);
-    unsigned* d = reinterpret_cast<unsigned*>(dst);
-    for (int i = threadIdx.x; i < static_cast<int>(sizeof(T) / 4); i += blockDim.x) d[i] = __ldcg(s + i);
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 template <int BITS, int G, int HD>
 __global__ void __launch_bounds__(kPsThreads, 1) decode_program_kernel(DecodeProgram* prog, int pos) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ GemvParams sg;
-    __shared__ AttnParams sa;
+    // the parameters of this layer and the next: one word per thread is loaded
+    // at the start of a layer and stored after its last phase, so no phase
+    // waits for its parameters
+    __shared__ DecodeLayer s_layer[2];
     __shared__ unsigned s_base;
     constexpr int kAttThreadsPs = 2 * kFaThreads;  // two warp groups
+    constexpr int kWords = static_cast<int>(sizeof(DecodeLayer) / 4);
+    static_assert(sizeof(DecodeLayer) % 4 == 0 && kWords <= kPsThreads, "one parameter word per thread");
     const int tid = threadIdx.x, cta = blockIdx.x, ctas = gridDim.x;
-    if (tid == 0) s_base = *reinterpret_cast<volatile unsigned*>(&prog->base);
-    __syncthreads();
-    const unsigned base = s_base;
     const DecodeLayer* layers = reinterpret_cast<const DecodeLayer*>(prog + 1);
     const int L = prog->layers, att_items = prog->att_items;
+    if (tid == 0) s_base = *reinterpret_cast<volatile unsigned*>(&prog->base);
+    if (tid < kWords)
+        reinterpret_cast<unsigned*>(&s_layer[0])[tid] = __ldcg(reinterpret_cast<const unsigned*>(&layers[0]) + tid);
+    __syncthreads();
+    const unsigned base = s_base;
     unsigned k = 0;  // barriers of this launch passed so far
     auto arrive = [&] {
         __syncthreads();
@@ -1902,33 +1957,30 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_program_kernel(DecodePro
         if (tid == 0) grid_spin(prog, base + k * static_cast<unsigned>(ctas));
         part_sync<kPsAttnSync, kAttThreadsPs>();
     };
-    auto gemv_phase = [&](const GemvParams& src, auto mode_tag, auto ring_tag) {
+    auto gemv_phase = [&](const GemvParams& p, auto mode_tag, auto ring_tag) {
         constexpr int MODE = decltype(mode_tag)::value, D = decltype(ring_tag)::value;
-        stage_params(&sg, &src);
-        __syncthreads();
-        if (tid == 0) sg.pos = pos;
-        __syncthreads();
-        gemv_sm_body<BITS, MODE, kPsThreads, D, true>(sg, smem, cta, ctas, wait_all);
+        constexpr int PRIME = D == kPsRing1 ? kPsPrime1 : kPsPrime2;
+        gemv_sm_body<BITS, MODE, kPsThreads, D, true, false, PRIME>(p, smem, cta, ctas, wait_all);
         arrive();
     };
     using One = std::integral_constant<int, kPsRing1>;
     using Two = std::integral_constant<int, kPsRing2>;
     for (int l = 0; l < L; ++l) {
-        const DecodeLayer& e = layers[l];
-        gemv_phase(e.qkv, std::integral_constant<int, kRopePairs>(), One());
-        // attention over tokens [0, pos]: the tiles of tokens before pos are
-        // requested before the barrier (only this layer's QKV phase writes pos)
-        stage_params(&sa, &e.att);
-        __syncthreads();
+        DecodeLayer& e = s_layer[l & 1];
+        const unsigned next = l + 1 < L && tid < kWords
+                                  ? __ldcg(reinterpret_cast<const unsigned*>(&layers[l + 1]) + tid)
+                                  : 0u;
         if (tid == 0) {
-            sa.ctx = pos + 1;
-            sa.stable = pos;
+            e.qkv.pos = pos;
+            e.att.ctx = pos + 1;  // attention over tokens [0, pos]
+            e.att.stable = pos;   // only this layer's QKV phase writes token pos
         }
         __syncthreads();
+        gemv_phase(e.qkv, std::integral_constant<int, kRopePairs>(), One());
         if (cta < att_items) {
             if (tid < kAttThreadsPs)
-                attention_fa_body<G, HD, kFaDeepStages, 1, 2, kPsAttnSync>(sa, smem, cta % sa.splits, cta / sa.splits,
-                                                                            wait_att);
+                attention_fa_body<G, HD, kFaDeepStages, 1, 2, kPsAttnSync>(e.att, smem, cta % e.att.splits,
+                                                                            cta / e.att.splits, wait_att);
         } else if (tid == 0) {
             grid_spin(prog, base + k * static_cast<unsigned>(ctas));
         }
@@ -1936,6 +1988,8 @@ __global__ void __launch_bounds__(kPsThreads, 1) decode_program_kernel(DecodePro
         gemv_phase(e.o, std::integral_constant<int, kGemv>(), One());
         gemv_phase(e.ffn, std::integral_constant<int, kSwiglu>(), Two());
         gemv_phase(e.down, std::integral_constant<int, kGemv>(), One());
+        if (l + 1 < L && tid < kWords) reinterpret_cast<unsigned*>(&s_layer[(l + 1) & 1])[tid] = next;
+        __syncthreads();  // the next layer's block is complete before thread 0 sets its position
     }
     if (cta == 0 && tid == 0) {
         // every CTA has arrived k times: the next launch starts from here
@@ -2398,6 +2452,7 @@ int vkc_decode_program_build(const vkc_decode_dims* dims, const vkc_decode_layer
         a.scale_log2 = kLog2e / sqrtf(static_cast<float>(hd));
         a.pitch = hd + 4;
         a.smem = static_cast<int>(prog->smem);
+        a.pre_max = kPsAttnPrime;
         // O projection + residual: x' = x + O attn
         L.o = base_params(w.o, w.o_scale, w.o_zero, d.hidden, q_rows);
         L.o.x = bufs->attn;
