@@ -54,8 +54,8 @@ void vkc_set_timing(int enable);
 int vkc_get_timing(void);
 /* Which kernel runs the single-vector GEMV family (vkc_gemv,
  * vkc_rmsnorm_gemv, -rope, -rope_kv, -swiglu, vkc_gemv_residual / _peer):
- * 0 (default) chooses per shape -- one CTA per SM (1024 threads for
- * single-stream 4-bit weights, 512 otherwise), each with a balanced range
+ * 0 (default) chooses per shape -- one CTA per SM (512 threads, leaving
+ * half of each SM to the next launch), each with a balanced range
  * of whole-K output columns, when every SM gets at least 16 outputs and the
  * input is not a peer exchange; otherwise clusters that split K and reduce in
  * distributed shared memory.  1 always uses the cluster

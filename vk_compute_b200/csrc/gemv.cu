@@ -1468,8 +1468,8 @@ int sm_count(int* out) {
 }
 
 // Which single-vector GEMV kernel runs (vkc_set_gemv_plan), per host thread:
-// 0 chooses per shape (the per-SM kernel's full-SM shape for single-stream
-// 4-bit weights, its half-SM shape otherwise), 1 always the cluster
+// 0 chooses per shape (the per-SM kernel in its half-SM shape where it
+// applies, else the cluster kernel), 1 always the cluster
 // split-K kernel, 2 the one-CTA-per-SM kernel in its full-SM shape wherever it
 // can run, 3 the same in its half-SM shape, 4 chooses per shape with the
 // full-SM shape.
@@ -1594,11 +1594,9 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
     if (g_gemv_plan != 1) {
-        // automatic shape, as measured on B200: 512 threads (the next launch
-        // primes its ring beside this one) except for single-stream 4-bit
-        // weights, whose short per-thread streams gain more from the 1024
-        // threads' bytes in flight
-        const bool half = g_gemv_plan == 3 || (g_gemv_plan == 0 && !(BITS == 4 && NS == 1));
+        // automatic shape, as measured on B200 for every width: 512 threads
+        // (the next launch primes its ring beside this one)
+        const bool half = g_gemv_plan == 3 || g_gemv_plan == 0;
         const SmShape sh = sm_shape(NS, p.K, half);
         if (sm_kernel_fits<BITS, MODE>(p, sms, sh)) return launch_sm<BITS, MODE>(p, stream, sms, sh);
     }
