@@ -179,9 +179,10 @@ def build_workload(name: str, rank: int, device, world: int = 1):
 
     if name == "rmsnorm_gemv_int8" and world > 1:
         # The 12288 x 4096 matrix row-sharded: rank r owns outputs
-        # [r*N/world, (r+1)*N/world) (whole 256-row scale blocks) and computes
-        # its slice of y; the library's NVLink peer all-gather then gives
-        # every rank the whole y (strong scaling: the job is fixed).
+        # [r*N/world, (r+1)*N/world) (whole 256-row scale blocks); its
+        # RmsNorm-GEMV stores them straight into every rank's copy of y over
+        # NVLink and a wait kernel returns once every rank's part has arrived
+        # (strong scaling: the job is fixed).
         from vk_compute_b200.p2p import PeerGather
 
         K, N, bits = 4096, 12288, 8
@@ -199,14 +200,14 @@ def build_workload(name: str, rank: int, device, world: int = 1):
         del shard
 
         def step(i):
-            ops.rmsnorm_gemv(pool[i % len(pool)], x, gamma, eps=1e-6, out=y_loc)
-            peer.gather("y", y_loc)
+            peer.rmsnorm_gemv_gather("y", pool[i % len(pool)], x, gamma, eps=1e-6)
 
         gemv = lambda i: ops.rmsnorm_gemv(pool[i % len(pool)], x, gamma, eps=1e-6, out=y_loc)
         job = K * N + 8 * K * N // 256 + 4 * K * 2 + 4 * N
         rank_bytes = wbytes + 4 * K * 2 + 4 * n_loc
         meta = {"K": K, "N": N, "bits": bits, "rows_per_rank": n_loc, "pool": len(pool),
-                "pool_bytes": len(pool) * wbytes, "exchange": "NVLink peer all-gather of y (vkc_allgather_p2p)"}
+                "pool_bytes": len(pool) * wbytes,
+                "exchange": "all-gather of y fused into the GEMV epilogue (NVLink peer stores) + one wait kernel"}
         return dict(step=step, bytes=rank_bytes, job_bytes=job, scaling="strong", launches=2, dominant=gemv,
                     dominant_bytes=rank_bytes, dominant_name=f"RmsNorm-GEMV-INT8 {n_loc}x{K} shard", meta=meta,
                     e2e=None, e2e_sharded=(x, peer.buffers["y"], K, N), kernels=[], close=peer.close)

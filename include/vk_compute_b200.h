@@ -347,6 +347,21 @@ int vkc_gemm_f32(const float* a, const float* b, float* c, int M, int N, int K, 
  * exceeds its bound sets flag 0x8 in *status (device memory) instead of hanging. */
 int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats,
                       int rank, int world, unsigned* status, void* stream);
+/* Row-sharded RmsNorm-GEMV whose epilogue stores the outputs straight into
+ * every rank's full vector (no counterpart in the reference): this rank's N
+ * outputs (its rows of the matrix) go to `offset` of each rank's vector (dsts:
+ * device array of `world` pointers, as for vkc_allgather_p2p; one-CTA-per-SM
+ * kernel).  vkc_gather_wait, launched next on the same stream, signals this
+ * rank's arrival on counter `rank` of every rank (counters: as for
+ * vkc_allgather_p2p; do not mix the two on one set of counters) and returns on
+ * the GPU once every rank's step-th launch has arrived here; step_word is a
+ * device word (zero at first) counting this rank's waits; a wait beyond its
+ * bound sets flag 0x8 in *status. */
+int vkc_rmsnorm_gemv_gather(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                            const float* gamma, void* const* dsts, int rank, int world, int offset, int N, int K,
+                            float eps, int rms_dim, void* stream);
+int vkc_gather_wait(unsigned* const* counters, int rank, int world, unsigned* step_word, unsigned* status,
+                    void* stream);
 /* All-reduce with residual for K-split projections (no counterpart in the
  * reference): `part` is this rank's partial output (n floats); it is stored
  * into slot `rank` of every rank's partial buffer (slots: device array of

@@ -143,6 +143,62 @@ def _gather_child(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
+def _gemv_gather_child(rank, world, port, out_dir):
+    """The row-sharded RmsNorm-GEMV with the gather in its epilogue: every
+    rank's copy of y equals the concatenation of the ranks' own shard outputs
+    (the same per-SM kernel computes both, so bit for bit), eager and from a
+    replayed graph."""
+    dist = _init(rank, world, port)
+    from vk_compute_b200 import ops
+    from vk_compute_b200.p2p import PeerGather
+
+    dev = torch.device("cuda", rank)
+    K, N = 4096, 12288
+    n_loc = N // world
+    wg = torch.Generator(device=dev).manual_seed(77)
+    full = torch.randn(K, N, generator=wg, device=dev) * 0.02
+    w = ops.pack_dense(full[:, rank * n_loc:(rank + 1) * n_loc].contiguous(), 8, symmetric=True, fp16_scale=True)
+    g = torch.Generator(device=dev).manual_seed(5)
+    gamma = 1 + 0.1 * torch.randn(K, generator=g, device=dev)
+    pg = PeerGather({"y": N}, dev)
+    bad = []
+    for it in range(3):
+        x = torch.randn(K, generator=g, device=dev)  # same stream of x on every rank
+        own = ops.rmsnorm_gemv(w, x, gamma, eps=1e-6)
+        parts = [torch.empty_like(own) for _ in range(world)]
+        dist.all_gather(parts, own)
+        if it < 2:
+            y = pg.rmsnorm_gemv_gather("y", w, x, gamma, eps=1e-6)
+        else:
+            graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.graph(graph, stream=s):
+                y = pg.rmsnorm_gemv_gather("y", w, x, gamma, eps=1e-6)
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if not torch.equal(y.cpu(), torch.cat(parts).cpu()):
+            bad.append(f"round {it}")
+        dist.barrier()
+        if it == 2:
+            del graph
+    if pg.timed_out():
+        bad.append("wait ran out")
+    pg.close()
+    with open(os.path.join(out_dir, f"ggather{rank}"), "w") as f:
+        f.write("ok" if not bad else "bad: " + ", ".join(bad))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@needs2
+def test_rmsnorm_gemv_gather_two_gpus():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_gemv_gather_child, 2, d)
+        for r in range(2):
+            assert open(os.path.join(d, f"ggather{r}")).read() == "ok"
+
+
 DECODE_CFG = dict(hidden=1024, inter=2048, n_q=8, n_kv=2, head_dim=128, layers=2, ctx=64)
 
 

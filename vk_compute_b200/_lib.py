@@ -30,6 +30,8 @@ SIGNATURES = {
     "vkc_get_gemv_int_dot": (_i, []),
     "vkc_set_attention_plan": (_i, [_i]),
     "vkc_get_attention_plan": (_i, []),
+    "vkc_rmsnorm_gemv_gather": (_i, [_i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _p]),
+    "vkc_gather_wait": (_i, [_p, _i, _i, _p, _p, _p]),
     "vkc_attention_plan_info": (_i, [_i, _i, _i, _i, C.POINTER(_i)]),
     "vkc_get_gemv_plan": (_i, []),
     "vkc_gemv": (_i, [_i, _p, _p, _p, _p, _p, _i, _i, _p]),

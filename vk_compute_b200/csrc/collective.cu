@@ -127,12 +127,60 @@ __global__ void __launch_bounds__(kGatherThreads) allreduce_residual_kernel(
     }
 }
 
+// Completion of a gathered GEMV (vkc_rmsnorm_gemv_gather), launched after it
+// on the same stream: once the GEMV has finished (its stores into every
+// rank's vector performed), one system fence and one arrival on counter `rank`
+// of every rank; then lanes wait, one source rank each, until every rank's
+// counter slot here has reached this wait's number (`step_word`, device,
+// counts this rank's waits), with acquire loads, bounded
+// (kStatusPeerTimeout on expiry).
+__global__ void __launch_bounds__(32) gather_wait_kernel(unsigned* const* ctrs, int rank, int world,
+                                                         unsigned* step_word, unsigned* status) {
+    __shared__ unsigned s_step;
+    pdl_wait();  // the GEMV's stores, and the previous wait's step
+    if (threadIdx.x == 0) {
+        s_step = *step_word + 1u;
+        *step_word = s_step;
+        fence_acq_rel_sys();  // the GEMV's stores (and the step) before the arrivals
+        for (int q = 0; q < world; ++q) red_add_relaxed_sys(ctrs[q] + rank, 1u);
+    }
+    __syncwarp();
+    const unsigned target = __shfl_sync(0xffffffffu, threadIdx.x == 0 ? s_step : 0u, 0);
+    pdl_launch_dependents();
+    const unsigned* mine = ctrs[rank];
+    for (int q = threadIdx.x; q < world; q += 32) {
+        const uint64_t deadline = globaltimer_ns() + kPeerWaitNs;
+        uint32_t it = 0;
+        while (static_cast<int>(ld_acquire_sys(mine + q) - target) < 0) {
+            if ((++it & 63u) == 0 && globaltimer_ns() > deadline) {
+                atomicOr(status, kStatusPeerTimeout);
+                break;
+            }
+        }
+    }
+}
+
 }  // namespace
 }  // namespace vkc
 
 using namespace vkc;
 
 extern "C" {
+
+int vkc_gather_wait(unsigned* const* counters, int rank, int world, unsigned* step_word, unsigned* status,
+                    void* stream) {
+    if (!counters || !step_word || !status) return set_error(kErrArg, "null gather-wait pointer");
+    if (world < 1 || world > 1024 || rank < 0 || rank >= world) return set_error(kErrArg, "rank %d of world %d", rank, world);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, 1);
+    cfg.blockDim = dim3(32, 1, 1);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[2];
+    cfg.attrs = attrs;
+    cfg.numAttrs = launch_attrs(attrs, 1);
+    VKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gather_wait_kernel, counters, rank, world, step_word, status));
+    return kOk;
+}
 
 int vkc_allgather_p2p(const float* src, void* const* dsts, unsigned* const* counters, int slice_floats, int rank,
                       int world, unsigned* status, void* stream) {

@@ -104,6 +104,12 @@ struct GemvParams {
     const unsigned long long* xslots;
     float* xsave;
     int prank, pworld;
+    // Gathered output (row-sharded GEMV): output j is stored at gather_off + j
+    // of every rank's full output vector (gather_dst: device array of pworld
+    // pointers, the peers' through NVLink); the arrival is signalled by the
+    // next kernel in the stream (vkc_gather_wait).
+    float* const* gather_dst;
+    int gather_off;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -239,6 +245,8 @@ __device__ __forceinline__ void finalize(const GemvParams& p, int j, bool active
             const unsigned flag = static_cast<unsigned>(__ldcg(p.peer_slots[p.prank] + e) >> 32) + 1u;
             const unsigned long long word = (static_cast<unsigned long long>(flag) << 32) | __float_as_uint(out);
             for (int q = 0; q < p.pworld; ++q) st_relaxed_sys_u64(p.peer_slots[q] + e, word);
+        } else if (p.gather_dst) {
+            for (int q = 0; q < p.pworld; ++q) p.gather_dst[q][p.gather_off + j] = out;
         } else {
             p.y[j] = out;
         }
@@ -1517,7 +1525,7 @@ SmShape sm_shape(int NS, int K, bool half) {
 // beside the ring, and the input is not a peer exchange (its per-element
 // waits would be repeated by every CTA).
 template <int BITS, int MODE>
-bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh) {
+bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh, bool force = false) {
     if (p.xslots || p.N % 2 != 0 || sh.smem > kSmMaxDynamicSmem) return false;
     // activations are read as 16-byte vectors
     auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
@@ -1528,7 +1536,7 @@ bool sm_kernel_fits(const GemvParams& p, int sms, const SmShape& sh) {
     // every CTA gets at least one pair of outputs, and at most T - 2 outputs
     if (BITS <= 8 && (p.N / kGroup > sms || (sms + p.N / kGroup - 1) / (p.N / kGroup) > kGroup / 2)) return false;
     if (BITS > 8 && (p.N / 2 < sms || p.N / sms > sh.T - 2)) return false;
-    if (g_gemv_plan == 2 || g_gemv_plan == 3) return true;
+    if (force || g_gemv_plan == 2 || g_gemv_plan == 3) return true;
     return p.N >= 16 * sms;
 }
 
@@ -1593,6 +1601,13 @@ int launch_one(const GemvParams& p0, cudaStream_t stream) {
     p.R = p.K / KPC;
     int sms = 0;
     if (int e = sm_count(&sms)) return e;
+    if (p.gather_dst) {
+        // gathered outputs: the per-SM kernel
+        const SmShape sh = sm_shape(NS, p.K, g_gemv_plan != 2 && g_gemv_plan != 4);
+        if (!sm_kernel_fits<BITS, MODE>(p, sms, sh, true))
+            return set_error(kErrUnsupported, "gathered GEMV: N=%d K=%d does not split over %d SMs", p.N, p.K, sms);
+        return launch_sm<BITS, MODE>(p, stream, sms, sh);
+    }
     if (g_gemv_plan != 1) {
         // automatic shape, as measured on B200 for every width: 512 threads
         // (the next launch primes its ring beside this one)
@@ -2223,6 +2238,32 @@ int vkc_rmsnorm_gemv_rope_kv_peer(int bits, const void* w, const float* scale, c
     if (!in) return set_error(kErrArg, "null peer input");
     return rope_kv_impl(bits, w, scale, zero, x_base, gamma, theta, y, N, K, eps, rms_dim, pos, head_dim, q_rows,
                         kv_rows, kv_layout, kcache, vcache, ctx_cap, stream, in);
+}
+
+int vkc_rmsnorm_gemv_gather(int bits, const void* w, const float* scale, const float* zero, const float* x,
+                            const float* gamma, void* const* dsts, int rank, int world, int offset, int N, int K,
+                            float eps, int rms_dim, void* stream) {
+    if (!gamma || !dsts) return set_error(kErrArg, "null gamma or destinations");
+    if (world < 1 || rank < 0 || rank >= world) return set_error(kErrArg, "rank %d of world %d", rank, world);
+    if (offset < 0) return set_error(kErrArg, "offset %d", offset);
+    if (rms_dim <= 0) return set_error(kErrArg, "rms_dim=%d must be positive", rms_dim);
+    float dummy = 0.f;  // y is unused: check_common only wants a non-null output
+    if (int e = check_common(bits, N, K, w, scale, zero, x, &dummy, gamma)) return e;
+    GemvParams p = {};
+    p.w[0] = static_cast<const uint8_t*>(w);
+    p.s[0] = scale;
+    p.z[0] = zero;
+    p.x = x;
+    p.gamma = gamma;
+    p.N = N;
+    p.K = K;
+    p.eps = eps;
+    p.inv_dim = 1.0f / static_cast<float>(rms_dim);
+    p.gather_dst = reinterpret_cast<float* const*>(dsts);
+    p.gather_off = offset;
+    p.prank = rank;
+    p.pworld = world;
+    return launch_mode<kRms>(bits, p, static_cast<cudaStream_t>(stream));
 }
 
 int vkc_rmsnorm_gemv(int bits, const void* w, const float* scale, const float* zero, const float* x,

@@ -67,6 +67,7 @@ class PeerGather:
                                          device=self.device) for n in names}
             self.ctr_ptrs = torch.tensor(self.peer_bases, dtype=torch.int64, device=self.device)
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._gather_step = None
             self._region = region
             torch.cuda.synchronize(self.device)
         dist.barrier(group=group)  # every rank has mapped every region (counters start at zero)
@@ -79,6 +80,28 @@ class PeerGather:
         st = torch.cuda.current_stream(self.device).cuda_stream
         check(lib().vkc_allgather_p2p(part.data_ptr(), self.dsts[name].data_ptr(), self.ctr_ptrs.data_ptr(), n,
                                       self.rank, self.world, self.status.data_ptr(), st))
+        return full
+
+    def rmsnorm_gemv_gather(self, name: str, w, x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-6,
+                            rms_dim: int | None = None) -> torch.Tensor:
+        """Row-sharded RmsNorm-GEMV with the all-gather in its epilogue
+        (vkc_rmsnorm_gemv_gather, then vkc_gather_wait): this rank's w (its
+        rows of the matrix, w.N outputs) writes its outputs at rank * w.N of
+        every rank's buffers[name]; returns buffers[name] once every rank's
+        part has arrived (on the GPU).  Uses the counters of this PeerGather:
+        do not mix with gather()/allreduce() on the same instance."""
+        full = self.buffers[name]
+        if full.numel() != w.N * self.world:
+            raise ValueError(f"{name}: {full.numel()} floats for {w.N} outputs x {self.world} ranks")
+        if self._gather_step is None:
+            self._gather_step = torch.zeros(1, dtype=torch.int32, device=self.device)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        check(lib().vkc_rmsnorm_gemv_gather(w.bits, w.packed.data_ptr(), ptr(w.scale), ptr(w.zero), x.data_ptr(),
+                                            gamma.data_ptr(), self.dsts[name].data_ptr(), self.rank, self.world,
+                                            self.rank * w.N, w.N, w.K, eps, rms_dim or w.K, st))
+        check(lib().vkc_gather_wait(self.ctr_ptrs.data_ptr(), self.rank, self.world, self._gather_step.data_ptr(),
+                                    self.status.data_ptr(), st))
         return full
 
     def allreduce(self, name: str, part: torch.Tensor, residual: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
