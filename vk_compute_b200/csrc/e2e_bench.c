@@ -4,8 +4,9 @@
  * memory, timed on the host clock.  Weights rotate through a pool larger than
  * four times the L2 cache so every step streams them from HBM.
  *
- *   vkc_e2e_bench <op> <N> <K> <steps> <warmup>
- *   op: RmsNorm-GEMV-INT8 | GEMV-FP16
+ *   vkc_e2e_bench <op> <N> <K> <steps> <warmup> [gemv_plan]
+ *   op: RmsNorm-GEMV-INT8 | GEMV-FP16; gemv_plan: vkc_set_gemv_plan's value
+ *   for the calling thread (default: the library's automatic choice)
  * The program never asks for getExecutionTime, so it turns execute()'s timing
  * events off (vkc_set_timing(0)), as such a program would.
  * Prints one JSON object: us_per_step, h2d_bytes_per_step, d2h_bytes_per_step,
@@ -55,6 +56,10 @@ int main(int argc, char** argv) {
     if (pool > 64) pool = 64;
 
     vkc_set_timing(0);
+    if (argc > 6 && vkc_set_gemv_plan(atoi(argv[6])) != 0) {
+        fprintf(stderr, "%s\n", vkc_last_error());
+        return 2;
+    }
     session s = createSession();
     uint8_t* hw = (uint8_t*)malloc(wbytes);
     float* hs = (float*)malloc(sbytes ? sbytes : 4);
