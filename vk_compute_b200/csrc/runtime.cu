@@ -6,8 +6,9 @@
 // freshly built pipeline per operation and waits on a fence
 // (src/dispatch.c:8-61).  Here an operation name selects a compiled sm_100a
 // launcher, its bindings are checked against the sizes the operator will
-// touch, the launches go onto the session stream between two timing events,
-// and execute() returns after the stream drains.  Fatal conditions print to
+// touch, and the launches go onto the session stream between two timing
+// events; results reach the host through readBuffer or getExecutionTime,
+// which wait for the stream.  Fatal conditions print to
 // stderr and exit, as every failure path of the reference does
 // (e.g. src/buffer.c:21-32, src/pipeline.c:9-11).
 #include "vkc_common.cuh"
@@ -17,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 extern "C" {
@@ -35,6 +37,9 @@ namespace vkc {
 
 static thread_local char g_err[512] = "";
 static bool g_pdl = false;
+// Programmatic dependent launch for the operation being enqueued by
+// execute(), whatever vkc_set_pdl says (set only where it is safe).
+static thread_local bool g_pdl_op = false;
 static bool g_timing = true;
 
 int set_error(int code, const char* fmt, ...) {
@@ -113,7 +118,7 @@ int launch_attrs(cudaLaunchAttribute* attrs, int cluster_x) {
     attrs[0].val.clusterDim.y = 1;
     attrs[0].val.clusterDim.z = 1;
     attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[1].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+    attrs[1].val.programmaticStreamSerializationAllowed = g_pdl || g_pdl_op ? 1 : 0;
     return 2;
 }
 
@@ -135,10 +140,35 @@ struct Ctx {
     int next;
     void* rstage;  // mapped pinned landing buffer for small reads
     void* rstage_dev;  // its device address
+    // Device ranges that work queued since the stream last drained may still
+    // write: staged uploads, and every binding of the operations enqueued
+    // (a superset of their outputs).  Past kPendingMax ranges, everything.
+    std::vector<std::pair<uintptr_t, size_t>> pending;
+    bool pending_all;
 };
+constexpr size_t kPendingMax = 64;
 constexpr size_t kStageMax = 1u << 20;  // larger uploads are copied synchronously
 
-void stream_synced(Ctx* c) { c->stage_busy[0] = c->stage_busy[1] = false; }
+void stream_synced(Ctx* c) {
+    c->stage_busy[0] = c->stage_busy[1] = false;
+    c->pending.clear();
+    c->pending_all = false;
+}
+
+void add_pending(Ctx* c, const void* p, size_t n) {
+    if (c->pending.size() >= kPendingMax)
+        c->pending_all = true;
+    else
+        c->pending.emplace_back(reinterpret_cast<uintptr_t>(p), n);
+}
+
+bool is_pending(const Ctx* c, const void* p, size_t n) {
+    if (c->pending_all) return true;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    for (const auto& r : c->pending)
+        if (a < r.first + r.second && r.first < a + n) return true;
+    return false;
+}
 
 // Copies between device memory and mapped pinned host memory for the small
 // buffers of readBuffer and writeBuffer: a kernel rather than a DMA copy
@@ -285,6 +315,30 @@ void need_bytes(const operation& op, int idx, int64_t bytes, const char* what) {
 }
 
 const void* dptr(const operation& op, int idx) { return op.buffers[idx].buffer; }
+
+// Whether an operation may start while the previous kernel of the stream
+// still runs (programmatic dependent launch).  The GEMV-family kernels read
+// their weights, scales, zeros and gamma before waiting for the previous
+// kernel and the activations (binding 0) after it; they may start early
+// when no binding but the activations can still be written by queued work
+// (an upload just staged by writeBuffer is the usual activation).
+bool early_reads_settled(const Ctx* c, const operation& op) {
+    const OpInfo* info = find_op(op.shader);
+    if (!info) return false;
+    switch (info->kind) {
+        case kOpGemv:
+        case kOpRmsGemv:
+        case kOpRope:
+        case kOpSwiglu:
+            break;
+        default:
+            return false;
+    }
+    for (int b = 1; b < op.bufferCount; ++b)
+        if (op.buffers[b].buffer && is_pending(c, op.buffers[b].buffer, static_cast<size_t>(op.buffers[b].size)))
+            return false;
+    return true;
+}
 
 void run_op(Ctx* c, const operation& op) {
     const OpInfo* info = find_op(op.shader);
@@ -596,6 +650,7 @@ void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
     if (n > kStageMax) {
         check_cuda(cudaMemcpyAsync(buf.buffer, data, n, cudaMemcpyHostToDevice, c->stream), "cudaMemcpyAsync");
         check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+        stream_synced(c);
         return;
     }
     // Two staging slots used in turn: a slot is reused only after the upload
@@ -615,11 +670,13 @@ void writeBuffer(VkDevice dev, VkQueue, buffer buf, const void* data) {
     memcpy(c->stage[slot], data, n);
     check_cuda(launch_copy16(buf.buffer, c->stage_dev[slot], n, c->stream), "upload kernel");
     c->stage_busy[slot] = true;
+    add_pending(c, buf.buffer, n);
 }
 
 void destroyBuffer(VkDevice dev, buffer buf) {
     Ctx* c = ctx_of(dev);
     check_cuda(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    stream_synced(c);
     if (buf.buffer) check_cuda(cudaFree(buf.buffer), "cudaFree");
 }
 
@@ -643,8 +700,13 @@ void execute(session s, operation ops[], int opCount) {
     for (int i = 0; i < opCount; ++i) {
         const bool last_full = plan == 0 && i == opCount - 1;
         if (last_full) vkc_set_gemv_plan(4);
+        g_pdl_op = early_reads_settled(c, ops[i]);
         run_op(c, ops[i]);
+        g_pdl_op = false;
         if (last_full) vkc_set_gemv_plan(plan);
+        for (int b = 0; b < ops[i].bufferCount; ++b)
+            if (ops[i].buffers[b].buffer)
+                add_pending(c, ops[i].buffers[b].buffer, static_cast<size_t>(ops[i].buffers[b].size));
     }
     if (timed) check_cuda(cudaEventRecord(c->ev_end, c->stream), "cudaEventRecord");
     check_cuda(cudaGetLastError(), "execute");
