@@ -190,3 +190,35 @@ def test_write_buffer_sequence_then_operator(sess):
         np.testing.assert_array_equal(D.read_buffer(sess, side[i]), xs[3 + i])
     for b in [xb, y, wb, sb, zb] + side:
         D.destroy_buffer(sess, b)
+
+
+def test_weights_rewritten_between_steps(sess):
+    """Weights, scales and x re-uploaded through the staged writeBuffer right
+    before each execute(), and a second operator whose gamma is the first
+    one's output: an operator that starts before the previous kernel ends
+    (programmatic dependent launch) reads weights early, so it may do so only
+    when no queued work can still write them.  Each step must see its own
+    weights, and the second operator the first one's result."""
+    x = host_vector(SEED_X, K)
+    wq = D.create_buffer(sess, None, K * K)  # int8 K x K, the first operator
+    sq = D.create_buffer(sess, None, 4 * K * (K // 256))
+    zq = D.create_buffer(sess, None, 4 * K * (K // 256))
+    w8 = D.create_buffer(sess, None, K * N)
+    s8 = D.create_buffer(sess, None, 4 * K * (N // 256))
+    z8 = D.create_buffer(sess, None, 4 * K * (N // 256))
+    xb, mid, y = D.create_buffer(sess, x), D.create_buffer(sess, None, 4 * K), D.create_buffer(sess, None, 4 * N)
+    for step in range(4):
+        dq, sqh, zqh = host_weight(SEED_W + 10 * step, K, K, 8)
+        d8, s8h, z8h = host_weight(SEED_W2 + 10 * step, K, N, 8)
+        xs = host_vector(SEED_X + step, K)
+        for b, a in ((wq, o.transpose_block16(dq, K, K, 8)), (sq, sqh), (zq, zqh),
+                     (w8, o.transpose_block16(d8, K, N, 8)), (s8, s8h), (z8, z8h), (xb, xs)):
+            D.write_buffer(sess, b, a)
+        D.execute(sess, [D.operation("GEMV-INT8.spv", [xb, wq, mid, sq, zq], [1, K, K]),
+                         D.operation("RmsNorm-GEMV-INT8.spv", [xb, mid, w8, y, s8, z8], [1, N, K])])
+        h = o.qgemv(xs, None, dq, sqh, zqh, 8, K, K)
+        ref = o.qgemv(xs, h, d8, s8h, z8h, 8, K, N, 4096, 1e-5)
+        assert_close(D.read_buffer(sess, mid), h, TOL[8], f"GEMV-INT8 step {step}")
+        assert_close(D.read_buffer(sess, y), ref, 5e-3, f"RmsNorm-GEMV-INT8 with gamma from the GEMV, step {step}")
+    for b in (wq, sq, zq, w8, s8, z8, xb, mid, y):
+        D.destroy_buffer(sess, b)
