@@ -891,7 +891,11 @@ def main():
         K, N = wl["meta"]["K"], wl["meta"]["N"]
         opname = "RmsNorm-GEMV-INT8" if args.workload == "rmsnorm_gemv_int8" else "GEMV-FP16"
         env = dict(os.environ, VKC_DEVICE=str(local))
-        out = subprocess.run([str(E2E_BIN), opname, str(N), str(K), str(args.steps), str(args.warmup)],
+        # host-clock steps of ~30 us: at least 1000 timed after 100 warm-up
+        # (well under a second), so that the first calls' one-time costs and
+        # scheduling noise do not weigh on the figure
+        e_steps, e_warm = max(args.steps, 1000), max(args.warmup, 100)
+        out = subprocess.run([str(E2E_BIN), opname, str(N), str(K), str(e_steps), str(e_warm)],
                              capture_output=True, text=True, env=env, timeout=600)
         if out.returncode != 0:
             raise RuntimeError(f"e2e host failed: {out.stderr[-400:]}")
@@ -903,7 +907,7 @@ def main():
             dt = float(tt.item())
         e2e = {"value": round(world * wl["bytes"] / dt / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": r["h2d_bytes_per_step"], "d2h_bytes_per_step": r["d2h_bytes_per_step"],
-               "us_per_step": round(dt * 1e6, 2),
+               "us_per_step": round(dt * 1e6, 2), "steps": e_steps, "warmup": e_warm,
                "host_us_per_call": {k: r.get("us_" + k) for k in ("write", "execute", "read")},
                "path": "C host (vkc_e2e_bench): writeBuffer + execute + readBuffer per step, reference ABI, "
                        "host wall clock, weight pool > 4x L2; execute timing events off (vkc_set_timing(0): "
