@@ -322,8 +322,7 @@ const void* dptr(const operation& op, int idx) { return op.buffers[idx].buffer; 
 // kernel and the activations (binding 0) after it; they may start early
 // when no binding but the activations can still be written by queued work
 // (an upload just staged by writeBuffer is the usual activation).
-bool early_reads_settled(const Ctx* c, const operation& op) {
-    const OpInfo* info = find_op(op.shader);
+bool early_reads_settled(const Ctx* c, const operation& op, const OpInfo* info) {
     if (!info) return false;
     switch (info->kind) {
         case kOpGemv:
@@ -340,8 +339,7 @@ bool early_reads_settled(const Ctx* c, const operation& op) {
     return true;
 }
 
-void run_op(Ctx* c, const operation& op) {
-    const OpInfo* info = find_op(op.shader);
+void run_op(Ctx* c, const operation& op, const OpInfo* info) {
     if (!info) fatal("unknown operator (shader) name: %s", op.shader);
     if (info->kind == kOpRmsNorm) {
         // No push constants: one workgroup per row of 256 (shader/RmsNorm.comp:5,22-23)
@@ -700,8 +698,9 @@ void execute(session s, operation ops[], int opCount) {
     for (int i = 0; i < opCount; ++i) {
         const bool last_full = plan == 0 && i == opCount - 1;
         if (last_full) vkc_set_gemv_plan(4);
-        g_pdl_op = early_reads_settled(c, ops[i]);
-        run_op(c, ops[i]);
+        const OpInfo* info = find_op(ops[i].shader);
+        g_pdl_op = early_reads_settled(c, ops[i], info);
+        run_op(c, ops[i], info);
         g_pdl_op = false;
         if (last_full) vkc_set_gemv_plan(plan);
         for (int b = 0; b < ops[i].bufferCount; ++b)
